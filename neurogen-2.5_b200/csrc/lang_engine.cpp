@@ -1,0 +1,452 @@
+// Host side of the language core: weight unpacking/transforms, device
+// layouts, and the per-token launch sequence.  Public C++ types keep the
+// reference's names (include/engine/*.h); the compute runs on the GPU with all
+// weights resident in HBM, uploaded once at construction.
+#include "engine/NeuralEngine.h"
+#include "lang_engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+namespace neurogen::cortical {
+
+// Unit tables from the laminar table: units are numbered layer by layer,
+// excitatory cells first within a layer.  Input goes to layer-4 excitatory
+// cells, feedback to layers 1, 5 and 6, and every excitatory cell is read out
+// (reference CorticalColumnV2 constructor, src/native/NeuralEngine.cpp:16-31).
+CorticalColumnV2::CorticalColumnV2(CorticalColumnConfig config) : config_(config) {
+  for (const LayerParams &lp : layers) {
+    const int cells = lp.excitatory + lp.inhibitory;
+    for (int k = 0; k < cells; ++k) {
+      const int unit = static_cast<int>(sign_.size());
+      const bool excitatory = k < lp.excitatory;
+      sign_.push_back(excitatory ? 1.f : -1.f);
+      layer_.push_back(lp.layer);
+      if (excitatory && lp.layer == 4) input_ids_.push_back(unit);
+      if (lp.layer == 1 || lp.layer >= 5) feedback_ids_.push_back(unit);
+      if (excitatory) output_ids_.push_back(unit);
+    }
+  }
+}
+
+// Packed parameters of one region, in stream order: recurrent c*64*64, input
+// weights+bias, feedback weights, output weights+bias, norm weight, norm
+// bias, memory decay (src/native/NeuralEngine.cpp:32-37, 57-64).
+size_t CorticalColumnV2::parameter_count() const {
+  const size_t c = config_.columns, w = config_.width;
+  return c * 64 * 64 + c * input_ids_.size() * (w + 1) + c * feedback_ids_.size() * w +
+         w * (c * output_ids_.size() * 2 + 1) + 3 * w;
+}
+
+} // namespace neurogen::cortical
+
+namespace ngb {
+using neurogen::cortical::CorticalColumnV2;
+using neurogen::cortical::EngineConfig;
+
+namespace {
+
+float sigmoid_host(float x) { return 1.f / (1.f + std::exp(-x)); }
+
+// 32-row panel layout used by the projection kernels:
+// W[m][k] -> out[(m/32)*K*32 + k*32 + m%32], rows padded with zeros.
+std::vector<float> to_panels(const float *W, size_t M, size_t K) {
+  const size_t P = (M + 31) / 32;
+  std::vector<float> out(P * K * 32, 0.f);
+  for (size_t m = 0; m < M; ++m)
+    for (size_t k = 0; k < K; ++k) out[(m / 32) * K * 32 + k * 32 + m % 32] = W[m * K + k];
+  return out;
+}
+
+DeviceBuffer upload(const float *host, size_t count) {
+  DeviceBuffer d(count * sizeof(float));
+  NGB_CUDA(cudaMemcpy(d.as<float>(), host, count * sizeof(float), cudaMemcpyHostToDevice));
+  return d;
+}
+DeviceBuffer upload(const std::vector<float> &v) { return upload(v.data(), v.size()); }
+
+} // namespace
+
+LangDims::LangDims(const EngineConfig &cfg, const CorticalColumnV2 &col)
+    : c(cfg.columns), w(cfg.width), R(cfg.regions), T(cfg.ticks), idle(cfg.idle_steps) {
+  n = c * 64;
+  n_in = static_cast<int>(col.input_ids().size());
+  n_fb = static_cast<int>(col.feedback_ids().size());
+  n_out = static_cast<int>(col.output_ids().size());
+  RS = 5L * n + w;
+  S = static_cast<long>(R) * RS;
+}
+
+void Scratch::ensure(const LangDims &d, int batch) {
+  if (batch <= capacity) return;
+  const size_t B = batch;
+  h.reset(B * d.w * 4);
+  hraw.reset(B * d.w * 4);
+  vin.reset(B * d.c * d.n_in * 4);
+  fb.reset(size_t(d.R) * B * d.c * d.n_fb * 4);
+  tr.reset(B * d.n * 4);
+  feat.reset(B * d.c * d.n_out * 2 * 4);
+  cnt.reset(B * (1 + d.idle) * d.R * sizeof(int));
+  tokens.reset(B * sizeof(int));
+  inputs.reset(B * d.w * 4);
+  state.reset(B * d.S * 4);
+  logits.reset(B * kVocab * 4);
+  hidden.reset(B * d.w * 4);
+  act.reset(B * 4);
+  capacity = batch;
+}
+
+DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, const float *data)
+    : dims(cfg, col) {
+  device = require_sm100_device();
+  label = device_label(device);
+  const LangDims &d = dims;
+  const size_t c = d.c, w = d.w;
+
+  // Unit tables for the kernels.
+  std::memset(&tables, 0, sizeof tables);
+  std::fill(std::begin(tables.in_idx), std::end(tables.in_idx), int8_t(-1));
+  std::fill(std::begin(tables.fb_idx), std::end(tables.fb_idx), int8_t(-1));
+  std::fill(std::begin(tables.out_idx), std::end(tables.out_idx), int8_t(-1));
+  for (int k = 0; k < d.n_in; ++k) tables.in_idx[col.input_ids()[k]] = int8_t(k);
+  for (int k = 0; k < d.n_fb; ++k) tables.fb_idx[col.feedback_ids()[k]] = int8_t(k);
+  for (int k = 0; k < d.n_out; ++k) tables.out_idx[col.output_ids()[k]] = int8_t(k);
+  for (int u = 0; u < 64; ++u)
+    if (col.sign()[u] > 0) tables.exc_mask |= 1ull << u;
+  tables.n_in = d.n_in;
+  tables.n_fb = d.n_fb;
+  tables.n_out = d.n_out;
+
+  // Recurrent connectivity mask: same layer, a preferred feed-forward pair, or
+  // an inhibitory presynaptic cell within one layer; no autapses
+  // (src/native/NeuralEngine.cpp:41-56, neurogen/language/model.py:42-48).
+  static const int preferred[6][2] = {{4, 2}, {4, 3}, {2, 3}, {3, 5}, {5, 6}, {6, 4}};
+  std::vector<float> rec_gain(64 * 64, 0.f);
+  for (int post = 0; post < 64; ++post)
+    for (int pre = 0; pre < 64; ++pre) {
+      const int lp = col.layer()[pre], lq = col.layer()[post];
+      bool ok = lp == lq;
+      for (const auto &pr : preferred) ok = ok || (lp == pr[0] && lq == pr[1]);
+      ok = ok || (col.sign()[pre] < 0 && std::abs(lq - lp) <= 1);
+      rec_gain[post * 64 + pre] = (ok && post != pre) ? col.sign()[pre] : 0.f;
+    }
+
+  const float *p = data;
+  auto take = [&](size_t count) {
+    const float *start = p;
+    p += count;
+    return start;
+  };
+  emb = upload(take(size_t(kVocab) * w), size_t(kVocab) * w);
+  regions.resize(d.R);
+  for (int r = 0; r < d.R; ++r) {
+    RegionWeights &g = regions[r];
+    // softplus(raw) * mask * sign, evaluated with the host libm exactly as the
+    // reference loader does (max(raw,0) + log1p(exp(-|raw|))).
+    const float *raw = take(c * 4096);
+    std::vector<float> rec(c * 4096);
+    for (size_t col_i = 0; col_i < c; ++col_i)
+      for (int k = 0; k < 4096; ++k) {
+        const float x = raw[col_i * 4096 + k];
+        const float gain = rec_gain[k];
+        rec[col_i * 4096 + k] =
+            gain != 0.f ? (std::max(x, 0.f) + std::log1p(std::exp(-std::abs(x)))) * gain : 0.f;
+      }
+    g.rec = upload(rec);
+    const float *in_w = take(c * d.n_in * w);
+    g.in_wp = upload(to_panels(in_w, c * d.n_in, w));
+    g.in_b = upload(take(c * d.n_in), c * d.n_in);
+    const float *fb_w = take(c * d.n_fb * w);
+    g.fb_wp = upload(to_panels(fb_w, c * d.n_fb, w));
+    const float *out_w = take(w * c * d.n_out * 2);
+    g.out_wp = upload(to_panels(out_w, w, c * d.n_out * 2));
+    g.out_b = upload(take(w), w);
+    g.norm_w = upload(take(w), w);
+    g.norm_b = upload(take(w), w);
+    const float *dec = take(w);
+    std::vector<float> decay(w);
+    for (size_t i = 0; i < w; ++i) decay[i] = .5f + .499f * sigmoid_host(dec[i]);
+    g.decay = upload(decay);
+  }
+  const float *head_w = take(size_t(kVocab) * w);
+  head_wp = upload(to_panels(head_w, kVocab, w));
+  head_b = upload(take(kVocab), kVocab);
+  NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+}
+
+DeviceModel::~DeviceModel() {
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, bool first_idle,
+                          int advances, float *d_state, float *d_logits, float *d_hidden,
+                          float *d_act, Scratch &sc, cudaStream_t st) const {
+  const LangDims &d = dims;
+  const int A = advances;
+  NGB_CUDA(cudaMemsetAsync(sc.cnt.as<int>(), 0, size_t(B) * A * d.R * sizeof(int), st));
+  const int Min = d.c * d.n_in, Mfb = d.c * d.n_fb, Kout = d.c * d.n_out * 2;
+  for (int adv = 0; adv < A; ++adv) {
+    const bool idle = adv > 0 || first_idle;
+    // Feedback projections of every region read only that region's memory,
+    // which the region updates after it has used them, so all regions'
+    // feedback for this advance can be computed up front.
+    for (int r = 0; r < d.R; ++r) {
+      ProjArgs fa{};
+      fa.wp = regions[r].fb_wp.as<float>();
+      fa.x = d_state + r * d.RS + 4L * d.n;
+      fa.ldx = d.S;
+      fa.y = sc.fb.as<float>() + size_t(r) * B * Mfb;
+      fa.ldy = Mfb;
+      fa.M = Mfb;
+      fa.K = d.w;
+      fa.B = B;
+      launch_projection(fa, st);
+    }
+    for (int r = 0; r < d.R; ++r) {
+      const RegionWeights &g = regions[r];
+      const bool sensory = !idle || r > 0;
+      const long roff = r * d.RS;
+      if (sensory) {
+        ProjArgs ia{};
+        ia.wp = g.in_wp.as<float>();
+        ia.bias = g.in_b.as<float>();
+        if (r == 0) {
+          ia.x = d_tokens ? emb.as<float>() : d_inputs;
+          ia.xidx = d_tokens;
+        } else {
+          ia.x = sc.h.as<float>();
+        }
+        ia.ldx = d.w;
+        ia.y = sc.vin.as<float>();
+        ia.ldy = Min;
+        ia.M = Min;
+        ia.K = d.w;
+        ia.B = B;
+        launch_projection(ia, st);
+      }
+      for (int t = 0; t < d.T; ++t) {
+        TickArgs ta{};
+        ta.rec = g.rec.as<float>();
+        ta.state = d_state;
+        ta.S = d.S;
+        ta.roff = roff;
+        ta.n = d.n;
+        ta.c = d.c;
+        ta.w = d.w;
+        ta.B = B;
+        float *state_trace = d_state + roff + d.n;
+        if (t % 2 == 0) {
+          ta.tr_in = state_trace;
+          ta.tr_in_ld = d.S;
+          ta.tr_out = sc.tr.as<float>();
+          ta.tr_out_ld = d.n;
+        } else {
+          ta.tr_in = sc.tr.as<float>();
+          ta.tr_in_ld = d.n;
+          ta.tr_out = state_trace;
+          ta.tr_out_ld = d.S;
+        }
+        ta.vin = sensory ? sc.vin.as<float>() : nullptr;
+        ta.fb = sc.fb.as<float>() + size_t(r) * B * Mfb;
+        ta.feat = t == d.T - 1 ? sc.feat.as<float>() : nullptr;
+        ta.spikes = sc.cnt.as<int>() + adv * d.R + r;
+        ta.spikes_ld = long(A) * d.R;
+        ta.tab = tables;
+        launch_tick(ta, st);
+      }
+      if (d.T % 2 == 1)
+        launch_copy_rows(sc.tr.as<float>(), d.n, d_state + roff + d.n, d.S, d.n, B, st);
+      ProjArgs oa{};
+      oa.wp = g.out_wp.as<float>();
+      oa.bias = g.out_b.as<float>();
+      oa.x = sc.feat.as<float>();
+      oa.ldx = Kout;
+      oa.y = sc.hraw.as<float>();
+      oa.ldy = d.w;
+      oa.addv = d_state + roff + 4L * d.n; // memory before this region's update
+      oa.ldadd = d.S;
+      oa.M = d.w;
+      oa.K = Kout;
+      oa.B = B;
+      launch_projection(oa, st);
+      NormArgs na{};
+      na.hraw = sc.hraw.as<float>();
+      na.hraw_ld = d.w;
+      na.h = sc.h.as<float>();
+      na.h_ld = d.w;
+      na.mem = d_state + roff + 4L * d.n;
+      na.mem_ld = d.S;
+      na.norm_w = g.norm_w.as<float>();
+      na.norm_b = g.norm_b.as<float>();
+      na.decay = g.decay.as<float>();
+      na.w = d.w;
+      na.B = B;
+      launch_norm(na, st);
+    }
+  }
+  if (d_logits) {
+    ProjArgs ha{};
+    ha.wp = head_wp.as<float>();
+    ha.bias = head_b.as<float>();
+    ha.x = sc.h.as<float>();
+    ha.ldx = d.w;
+    ha.y = d_logits;
+    ha.ldy = kVocab;
+    ha.M = kVocab;
+    ha.K = d.w;
+    ha.B = B;
+    launch_projection(ha, st);
+  }
+  if (d_hidden)
+    NGB_CUDA(cudaMemcpyAsync(d_hidden, sc.h.as<float>(), size_t(B) * d.w * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_act) launch_activity(sc.cnt.as<int>(), A, d.R, d.n, d.T, d_act, B, st);
+  NGB_CUDA(cudaGetLastError());
+}
+
+} // namespace ngb
+
+namespace neurogen::cortical {
+using namespace ngb;
+
+namespace {
+void validate_dims(const EngineConfig &c) {
+  if (c.columns < 1 || c.columns > 4096 || c.width < 1 || c.width > 16384 || c.regions < 1 ||
+      c.regions > 128 || c.ticks < 1 || c.ticks > 10000 || c.idle_steps < 0 || c.idle_steps > 16)
+    throw std::invalid_argument("Invalid native model dimensions");
+}
+bool all_finite(const float *p, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (!std::isfinite(p[i])) return false;
+  return true;
+}
+} // namespace
+
+NeuralEngine::NeuralEngine(EngineConfig c, const float *data, size_t count, const std::string &backend)
+    : config(c) {
+  validate_dims(c);
+  if (!data || count != parameter_count())
+    throw std::invalid_argument("Native weight count does not match architecture");
+  if (!all_finite(data, count)) throw std::invalid_argument("Non-finite weights");
+  if (backend != "cuda")
+    throw std::invalid_argument("Native backend '" + backend +
+                                "' unavailable; this library provides only 'cuda' "
+                                "(B200, sm_100a) (no silent fallback)");
+  CorticalColumnV2 column({c.columns, c.width, c.ticks});
+  impl_ = std::make_unique<DeviceModel>(c, column, data);
+}
+
+NeuralEngine::~NeuralEngine() = default;
+
+size_t NeuralEngine::parameter_count() const {
+  CorticalColumnV2 column({config.columns, config.width, config.ticks});
+  return 528ull * config.width + kVocab + size_t(config.regions) * column.parameter_count();
+}
+
+size_t NeuralEngine::state_size() const {
+  return size_t(config.regions) * (5ull * config.columns * 64 + config.width);
+}
+
+std::string NeuralEngine::backend_name() const { return impl_->label; }
+
+std::vector<ColumnState> NeuralEngine::unpack(const float *source) const {
+  std::vector<ColumnState> out;
+  const size_t n = size_t(config.columns) * 64, w = config.width;
+  for (int r = 0; r < config.regions; ++r) {
+    out.emplace_back(n, w);
+    ColumnState &s = out.back();
+    // Packed order per region: voltage, trace, adaptation, last_spikes,
+    // memory, counts (src/native/NeuralEngine.cpp:145-151).
+    for (std::vector<float> *f : {&s.neurons.voltage, &s.neurons.trace, &s.neurons.adaptation,
+                                  &s.neurons.last_spikes, &s.memory, &s.neurons.counts}) {
+      std::copy(source, source + f->size(), f->begin());
+      source += f->size();
+    }
+  }
+  return out;
+}
+
+void NeuralEngine::pack(const std::vector<ColumnState> &states, float *dest) const {
+  for (const ColumnState &s : states)
+    for (const std::vector<float> *f : {&s.neurons.voltage, &s.neurons.trace, &s.neurons.adaptation,
+                                        &s.neurons.last_spikes, &s.memory, &s.neurons.counts}) {
+      std::copy(f->begin(), f->end(), dest);
+      dest += f->size();
+    }
+}
+
+void NeuralEngine::step_batch(const int *tokens, int batch, const float *state, float *next_state,
+                              float *logits, float *hidden, float *activity) {
+  if (batch < 1) throw std::invalid_argument("Need at least one batch item");
+  if (!tokens || !state || !next_state) throw std::invalid_argument("Null input/output");
+  const size_t S = state_size();
+  if (!all_finite(state, S * batch)) throw std::invalid_argument("Non-finite native state");
+  for (int b = 0; b < batch; ++b)
+    if (tokens[b] < 0 || tokens[b] >= kVocab) throw std::invalid_argument("Token must be in 0..263");
+  DeviceModel &m = *impl_;
+  NGB_CUDA(cudaSetDevice(m.device));
+  Scratch &sc = m.host_scratch;
+  sc.ensure(m.dims, batch);
+  cudaStream_t st = m.stream;
+  NGB_CUDA(cudaMemcpyAsync(sc.tokens.as<int>(), tokens, batch * sizeof(int), cudaMemcpyHostToDevice, st));
+  NGB_CUDA(cudaMemcpyAsync(sc.state.as<float>(), state, S * batch * 4, cudaMemcpyHostToDevice, st));
+  m.enqueue(batch, sc.tokens.as<int>(), nullptr, false, 1 + config.idle_steps, sc.state.as<float>(),
+            sc.logits.as<float>(), sc.hidden.as<float>(), sc.act.as<float>(), sc, st);
+  NGB_CUDA(cudaMemcpyAsync(next_state, sc.state.as<float>(), S * batch * 4, cudaMemcpyDeviceToHost, st));
+  if (logits)
+    NGB_CUDA(cudaMemcpyAsync(logits, sc.logits.as<float>(), size_t(batch) * kVocab * 4, cudaMemcpyDeviceToHost, st));
+  if (hidden)
+    NGB_CUDA(cudaMemcpyAsync(hidden, sc.hidden.as<float>(), size_t(batch) * config.width * 4, cudaMemcpyDeviceToHost, st));
+  if (activity)
+    NGB_CUDA(cudaMemcpyAsync(activity, sc.act.as<float>(), size_t(batch) * 4, cudaMemcpyDeviceToHost, st));
+  NGB_CUDA(cudaStreamSynchronize(st));
+}
+
+void NeuralEngine::advance_batch(const float *inputs, int batch, const float *state, bool idle,
+                                 float *next_state, float *hidden, float *activity) {
+  if (batch < 1) throw std::invalid_argument("Need at least one batch item");
+  if (!inputs || !state || !next_state) throw std::invalid_argument("Null input/output");
+  const size_t S = state_size();
+  if (!all_finite(state, S * batch)) throw std::invalid_argument("Non-finite native state");
+  if (!all_finite(inputs, size_t(config.width) * batch)) throw std::invalid_argument("Non-finite input");
+  DeviceModel &m = *impl_;
+  NGB_CUDA(cudaSetDevice(m.device));
+  Scratch &sc = m.host_scratch;
+  sc.ensure(m.dims, batch);
+  cudaStream_t st = m.stream;
+  NGB_CUDA(cudaMemcpyAsync(sc.inputs.as<float>(), inputs, size_t(batch) * config.width * 4, cudaMemcpyHostToDevice, st));
+  NGB_CUDA(cudaMemcpyAsync(sc.state.as<float>(), state, S * batch * 4, cudaMemcpyHostToDevice, st));
+  m.enqueue(batch, nullptr, sc.inputs.as<float>(), idle, 1, sc.state.as<float>(), nullptr,
+            sc.hidden.as<float>(), sc.act.as<float>(), sc, st);
+  NGB_CUDA(cudaMemcpyAsync(next_state, sc.state.as<float>(), S * batch * 4, cudaMemcpyDeviceToHost, st));
+  if (hidden)
+    NGB_CUDA(cudaMemcpyAsync(hidden, sc.hidden.as<float>(), size_t(batch) * config.width * 4, cudaMemcpyDeviceToHost, st));
+  if (activity)
+    NGB_CUDA(cudaMemcpyAsync(activity, sc.act.as<float>(), size_t(batch) * 4, cudaMemcpyDeviceToHost, st));
+  NGB_CUDA(cudaStreamSynchronize(st));
+}
+
+Vector NeuralEngine::step(int token, std::vector<ColumnState> &state, Vector &hidden, float &activity) {
+  if (token < 0 || token >= kVocab) throw std::invalid_argument("Token must be in 0..263");
+  std::vector<float> packed(state_size());
+  pack(state, packed.data());
+  Vector logits(kVocab);
+  hidden.assign(config.width, 0.f);
+  step_batch(&token, 1, packed.data(), packed.data(), logits.data(), hidden.data(), &activity);
+  state = unpack(packed.data());
+  return logits;
+}
+
+Vector NeuralEngine::advance(const Vector &input, std::vector<ColumnState> &state, bool idle,
+                             float &activity) {
+  if (input.size() != size_t(config.width)) throw std::invalid_argument("Invalid native input size");
+  std::vector<float> packed(state_size());
+  pack(state, packed.data());
+  Vector hidden(config.width);
+  advance_batch(input.data(), 1, packed.data(), idle, packed.data(), hidden.data(), &activity);
+  state = unpack(packed.data());
+  return hidden;
+}
+
+} // namespace neurogen::cortical

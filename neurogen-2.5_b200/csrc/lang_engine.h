@@ -1,0 +1,65 @@
+// Device-resident language model: dims, weights in HBM, scratch, and the
+// launch sequence of one token / one advance for a batch of sessions.
+#pragma once
+#include "common.h"
+#include "engine/NeuralEngine.h"
+#include "lang_kernels.h"
+
+#include <string>
+#include <vector>
+
+namespace ngb {
+
+constexpr int kVocab = 264; // bytes + 8 control tokens (neurogen/language/model.py:16-17)
+
+struct LangDims {
+  LangDims(const neurogen::cortical::EngineConfig &cfg, const neurogen::cortical::CorticalColumnV2 &col);
+  int c, w, R, T, idle;
+  int n;                 // units per region (c*64)
+  int n_in, n_fb, n_out; // 12, 29, 50 per column
+  long RS;               // floats per region state block: 5n + w
+  long S;                // floats per session state: R * RS
+};
+
+struct RegionWeights {
+  DeviceBuffer rec;                     // [c][64][64], transformed
+  DeviceBuffer in_wp, in_b;             // panels of [c*n_in][w], bias
+  DeviceBuffer fb_wp;                   // panels of [c*n_fb][w]
+  DeviceBuffer out_wp, out_b;           // panels of [w][c*n_out*2], bias
+  DeviceBuffer norm_w, norm_b, decay;   // [w]
+};
+
+// Per-call device workspace for `capacity` sessions.
+struct Scratch {
+  int capacity = 0;
+  DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act;
+  void ensure(const LangDims &d, int batch);
+};
+
+class DeviceModel {
+public:
+  DeviceModel(const neurogen::cortical::EngineConfig &cfg,
+              const neurogen::cortical::CorticalColumnV2 &col, const float *packed);
+  ~DeviceModel();
+  DeviceModel(const DeviceModel &) = delete;
+  DeviceModel &operator=(const DeviceModel &) = delete;
+
+  // Enqueue `advances` advances of B sessions whose state [B][S] is on the
+  // device and is updated in place.  The first advance reads the embedding
+  // rows d_tokens (token step) or the inputs d_inputs [B][w]; it is idle when
+  // first_idle is set.  Outputs may be null.
+  void enqueue(int B, const int *d_tokens, const float *d_inputs, bool first_idle, int advances,
+               float *d_state, float *d_logits, float *d_hidden, float *d_act, Scratch &sc,
+               cudaStream_t st) const;
+
+  LangDims dims;
+  int device = 0;
+  std::string label;
+  cudaStream_t stream = nullptr;
+  UnitTables tables;
+  DeviceBuffer emb, head_wp, head_b;
+  std::vector<RegionWeights> regions;
+  Scratch host_scratch; // used by the host-buffer entry points (under the engine mutex)
+};
+
+} // namespace ngb

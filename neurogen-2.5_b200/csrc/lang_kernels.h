@@ -1,0 +1,83 @@
+// Launch interface of the language-core kernels (lang_kernels.cu).  Plain
+// structs of device pointers and sizes; the host engine (lang_engine.cpp)
+// builds them.  All kernels reproduce the reference CPU engine's fp32
+// arithmetic operation by operation (see lang_kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ngb {
+
+// Unit tables of a 64-unit column (derived from the laminar table,
+// include/engine/ALIFNeuron.h): index of each unit in the input / feedback /
+// output id lists, or -1, and a bitmask of excitatory units.
+struct UnitTables {
+  int8_t in_idx[64], fb_idx[64], out_idx[64];
+  uint64_t exc_mask;
+  int n_in, n_fb, n_out;
+};
+
+// y[b][m] = bias[m] + sum_{k=0..K-1, in order} W[m][k] * x[b][k]
+//           (+ 0.25f * addv[b][m] when addv is set)
+// W is stored in 32-row panels: W[m][k] at wp[(m/32)*K*32 + k*32 + m%32].
+// Row b of x is x + (xidx ? xidx[b] : b) * ldx.
+struct ProjArgs {
+  const float *wp;
+  const float *bias; // [M] or null
+  const float *x;
+  const int *xidx; // optional row gather (embedding lookup)
+  long ldx;
+  float *y;
+  long ldy;
+  const float *addv; // optional 0.25 * addv epilogue
+  long ldadd;
+  int M, K, B;
+};
+void launch_projection(const ProjArgs &a, cudaStream_t s);
+
+// One synchronous recurrent ALIF tick of one region for B sessions
+// (reference CPUBackend.cpp:20-42 with the input current assembled as in
+// NeuralEngine.cpp:72-86).  State block of session b, this region:
+// state + b*S + roff : [V n][trace n][adapt n][last n][memory w][counts n].
+struct TickArgs {
+  const float *rec; // [c][64][64] transformed recurrent weights
+  float *state;
+  long S, roff;
+  int n, c, w, B;
+  const float *tr_in; // previous trace, per session stride tr_in_ld
+  long tr_in_ld;
+  float *tr_out;
+  long tr_out_ld;
+  const float *vin; // input projection [B][c*n_in] or null (non-sensory)
+  const float *fb;  // feedback projection [B][c*n_fb]
+  float *feat;      // [B][c*n_out*2] written when non-null (last tick)
+  int *spikes;      // spike counter per session, stride spikes_ld
+  long spikes_ld;
+  UnitTables tab;
+};
+void launch_tick(const TickArgs &a, cudaStream_t s);
+
+// Copy trace src (stride src_ld) -> dst (stride dst_ld), n floats per session.
+void launch_copy_rows(const float *src, long src_ld, float *dst, long dst_ld,
+                      int n, int B, cudaStream_t s);
+
+// h = LayerNorm(hraw) * norm_w + norm_b (mean/variance in fp64), then
+// memory = decay * memory + (1 - decay) * h  (NeuralEngine.cpp:96-108).
+struct NormArgs {
+  const float *hraw;
+  long hraw_ld;
+  float *h;
+  long h_ld;
+  float *mem;
+  long mem_ld;
+  const float *norm_w, *norm_b, *decay;
+  int w, B;
+};
+void launch_norm(const NormArgs &a, cudaStream_t s);
+
+// activity[b] from integer spike counts [B][A][R]
+// (PackedBackend.h:50-53, NeuralEngine.cpp:164-189).
+void launch_activity(const int *counts, int A, int R, int n, int T, float *act,
+                     int B, cudaStream_t s);
+
+} // namespace ngb

@@ -1,0 +1,613 @@
+// Isolated-tick spiking network: seeded topology generation, CSR / 16x16-block
+// layouts by presynaptic neuron, device state and the tick loop.
+//
+// Generated inputs (3, 5) are deterministic functions of
+// the seed through a counter-based generator (splitmix64 of (stream, a, b)),
+// so any machine and any thread count produce the same network.  Weights are
+// rounded onto the delay ring's fixed-point grid (multiples of 2^-24 nS):
+// fp16 weights already are; fp32 weights are rounded once at generation.
+#include "net_engine.h"
+
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace ngb {
+namespace {
+
+inline uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Independent counter-based streams: value(a, b) for a, b < 2^32.
+struct Stream {
+  uint64_t key;
+  Stream(uint64_t seed, uint64_t id) : key(mix64(seed ^ mix64(id))) {}
+  uint64_t bits(uint64_t a, uint64_t b) const { return mix64(((a << 32) | (b & 0xFFFFFFFFull)) ^ key); }
+  double uniform(uint64_t a, uint64_t b) const { return double(bits(a, b) >> 11) * 0x1.0p-53; }
+  // Uniform integer in [0, m).
+  uint64_t below(uint64_t a, uint64_t b, uint64_t m) const {
+    return (uint64_t)((unsigned __int128)bits(a, b) * m >> 64);
+  }
+};
+
+enum : uint64_t { S_EDGE = 1, S_PRE, S_DELAY, S_W1, S_W2, S_BLOCK, S_FILL };
+
+struct WeightDraw {
+  const ng_net_config &c;
+  Stream w1, w2;
+  explicit WeightDraw(const ng_net_config &cfg) : c(cfg), w1(cfg.seed, S_W1), w2(cfg.seed, S_W2) {}
+  double normal(uint64_t a, uint64_t b) const {
+    const double u1 = (double((w1.bits(a, b) >> 11) + 1)) * 0x1.0p-53; // (0, 1]
+    const double u2 = w2.uniform(a, b);
+    return std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2);
+  }
+  // Signed weight keyed by (a, b); inhibitory presynaptic cells are negative.
+  // Returns fp32 value and, for fp16 storage, the fp16 bits.
+  float draw(uint64_t a, uint64_t b, bool inhibitory, uint16_t *half_bits) const {
+    const double z = normal(a, b);
+    if (c.weight_kind == NG_W_LOGNORMAL_F32) {
+      const double w = std::exp(double(c.w_mu) + double(c.w_sigma) * z);
+      float q = float(std::nearbyint(w * 16777216.0) * 0x1.0p-24);
+      if (q == 0.f) q = 0x1.0p-24f;
+      return inhibitory ? -q : q;
+    }
+    float m = float(std::fabs(double(c.w_sigma) * z));
+    __half h = __float2half_rn(m);
+    if (__half2float(h) == 0.f) h = __ushort_as_half(1); // smallest subnormal, 2^-24
+    uint16_t bits = __half_as_ushort(h);
+    if (inhibitory) bits |= 0x8000u;
+    if (half_bits) *half_bits = bits;
+    return __half2float(__ushort_as_half(bits));
+  }
+};
+
+inline uint32_t pack_word(int post, int delay) { return uint32_t(post) | (uint32_t(delay - 1) << 28); }
+
+long long pad8(long long x) { return (x + 7) & ~7LL; }
+
+// Per-postsynaptic-neuron bound on the summed fixed-point input of one slot.
+void check_ring_bound(int n, const std::vector<double> &sum_e, const std::vector<double> &sum_i) {
+  for (int j = 0; j < n; ++j)
+    if (sum_e[j] >= 127.0 || sum_i[j] >= 127.0)
+      throw std::invalid_argument("Synaptic input of neuron " + std::to_string(j) +
+                                  " can exceed the delay ring's fixed-point range (127 nS per slot)");
+}
+
+void finish_rows(HostCSR &out, const std::vector<long long> &count) {
+  const int n = out.n;
+  out.row.assign(size_t(n) + 1, 0);
+  for (int i = 0; i < n; ++i) out.row[i + 1] = out.row[i] + pad8(count[i]);
+  const size_t total = size_t(out.row[n]);
+  out.syn.assign(total, pack_word(0, 1));
+  out.outdeg.assign(n, 0);
+}
+
+} // namespace
+
+void validate_config(const ng_net_config &c) {
+  if (c.n < 1 || c.n > int(kPostMask)) throw std::invalid_argument("Network size must be in 1..2^28-1");
+  if (c.n_exc < 0 || c.n_exc > c.n) throw std::invalid_argument("n_exc must be in 0..n");
+  if (c.delay_min < 1 || c.delay_max < c.delay_min || c.delay_max > kRingSlots - 1)
+    throw std::invalid_argument("Delays must satisfy 1 <= delay_min <= delay_max <= 15");
+  if (c.weight_kind != NG_W_LOGNORMAL_F32 && c.weight_kind != NG_W_HALFNORMAL_F16)
+    throw std::invalid_argument("Unknown weight kind");
+  if (!(c.dt_ms > 0) || !(c.cap_exc_pf > 0) || !(c.cap_inh_pf > 0) || !(c.g_leak_ns > 0) ||
+      !(c.tau_exc_ms > 0) || !(c.tau_inh_ms > 0) || !(c.tau_adapt_ms > 0) || !(c.t_ref_ms >= 0))
+    throw std::invalid_argument("Membrane constants must be positive");
+  const float vals[] = {c.e_leak_mv, c.e_inh_mv, c.v_thresh_mv, c.v_reset_mv, c.adapt_inc_pa, c.bias_pa,
+                        c.drive_p, c.drive_ns, c.p_connect, c.w_mu, c.w_sigma};
+  for (float v : vals)
+    if (!std::isfinite(v)) throw std::invalid_argument("Network parameters must be finite");
+  if (c.drive_kind != NG_DRIVE_CONDUCTANCE && c.drive_kind != NG_DRIVE_IMPOSED)
+    throw std::invalid_argument("Unknown drive kind");
+  if (c.drive_p < 0 || c.drive_p > 1) throw std::invalid_argument("drive_p must be in [0, 1]");
+  if (c.storage != 0 && c.storage != 1) throw std::invalid_argument("storage must be 0 (CSR) or 1 (BSR)");
+  switch (c.topology) {
+  case NG_TOPO_ERDOS_RENYI:
+    if (!(c.p_connect >= 0 && c.p_connect <= 1)) throw std::invalid_argument("p_connect must be in [0, 1]");
+    break;
+  case NG_TOPO_FIXED_FANIN:
+    if (c.fanin < 0 || c.n < 2) throw std::invalid_argument("fixed fan-in needs fanin >= 0 and n >= 2");
+    break;
+  case NG_TOPO_BSR16:
+    if (c.n % 16) throw std::invalid_argument("16x16 block topology needs n divisible by 16");
+    if (c.bsr_blocks < 0 || c.bsr_blocks > c.n / 16) throw std::invalid_argument("bsr_blocks out of range");
+    if (c.bsr_fill < 1 || c.bsr_fill > 256) throw std::invalid_argument("bsr_fill must be in 1..256");
+    if (c.weight_kind != NG_W_HALFNORMAL_F16) throw std::invalid_argument("16x16 blocks store fp16 weights");
+    break;
+  default:
+    throw std::invalid_argument("Unknown topology");
+  }
+  if (c.storage == 1 && c.topology != NG_TOPO_BSR16)
+    throw std::invalid_argument("Block storage needs the 16x16 block topology");
+}
+
+// ---------------------------------------------------------------------------
+// CSR generation.
+// ---------------------------------------------------------------------------
+void generate_csr(const ng_net_config &c, HostCSR &out) {
+  const int n = c.n;
+  out.n = n;
+  const WeightDraw wd(c);
+  const Stream edge(c.seed, S_EDGE), pres(c.seed, S_PRE), dly(c.seed, S_DELAY);
+  const uint64_t dspan = uint64_t(c.delay_max - c.delay_min + 1);
+  const bool half = c.weight_kind == NG_W_HALFNORMAL_F16;
+  std::vector<double> sum_e(n, 0.0), sum_i(n, 0.0);
+
+  if (c.topology == NG_TOPO_ERDOS_RENYI) {
+    // Row by row (presynaptic), posts in ascending order.
+    std::vector<long long> count(n, 0);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int i = 0; i < n; ++i) {
+      long long k = 0;
+      for (int j = 0; j < n; ++j)
+        if (j != i && edge.uniform(uint64_t(i), uint64_t(j)) < double(c.p_connect)) ++k;
+      count[i] = k;
+    }
+    finish_rows(out, count);
+    if (half) out.w16.assign(out.syn.size(), 0);
+    else out.w32.assign(out.syn.size(), 0.f);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int i = 0; i < n; ++i) {
+      long long e = out.row[i];
+      const bool inh = i >= c.n_exc;
+      for (int j = 0; j < n; ++j) {
+        if (j == i || !(edge.uniform(uint64_t(i), uint64_t(j)) < double(c.p_connect))) continue;
+        const int d = c.delay_min + int(dly.below(uint64_t(i), uint64_t(j), dspan));
+        out.syn[e] = pack_word(j, d);
+        uint16_t hb = 0;
+        const float w = wd.draw(uint64_t(i), uint64_t(j), inh, &hb);
+        if (half) out.w16[e] = hb;
+        else out.w32[e] = w;
+        ++e;
+      }
+      out.outdeg[i] = int(count[i]);
+    }
+    for (int i = 0; i < n; ++i)
+      for (long long e = out.row[i]; e < out.row[i] + out.outdeg[i]; ++e) {
+        const double w = half ? double(__half2float(__ushort_as_half(out.w16[e]))) : double(out.w32[e]);
+        (w < 0 ? sum_i : sum_e)[out.syn[e] & kPostMask] += std::fabs(w);
+      }
+  } else if (c.topology == NG_TOPO_FIXED_FANIN) {
+    // Each post draws `fanin` uniform presynaptic cells (no autapse: a draw of
+    // the post itself moves to the next cell), then a stable scatter by pre.
+    const int K = c.fanin;
+    const size_t total = size_t(n) * K;
+    std::vector<int> tpre(total);
+    std::vector<uint32_t> tword(total);
+    std::vector<float> tw32(half ? 0 : total);
+    std::vector<uint16_t> tw16(half ? total : 0);
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; ++j)
+      for (int k = 0; k < K; ++k) {
+        int pre = int(pres.below(uint64_t(j), uint64_t(k), uint64_t(n)));
+        if (pre == j) pre = (pre + 1) % n;
+        const size_t x = size_t(j) * K + k;
+        tpre[x] = pre;
+        tword[x] = pack_word(j, c.delay_min + int(dly.below(uint64_t(j), uint64_t(k), dspan)));
+        uint16_t hb = 0;
+        const float w = wd.draw(uint64_t(j), uint64_t(k), pre >= c.n_exc, &hb);
+        if (half) tw16[x] = hb;
+        else tw32[x] = w;
+      }
+    std::vector<long long> count(n, 0);
+    for (size_t x = 0; x < total; ++x) ++count[tpre[x]];
+    finish_rows(out, count);
+    if (half) out.w16.assign(out.syn.size(), 0);
+    else out.w32.assign(out.syn.size(), 0.f);
+    std::vector<long long> fill(out.row.begin(), out.row.end() - 1);
+    for (size_t x = 0; x < total; ++x) {
+      const long long e = fill[tpre[x]]++;
+      out.syn[e] = tword[x];
+      if (half) out.w16[e] = tw16[x];
+      else out.w32[e] = tw32[x];
+      const double w = half ? double(__half2float(__ushort_as_half(tw16[x]))) : double(tw32[x]);
+      (w < 0 ? sum_i : sum_e)[x / K] += std::fabs(w);
+    }
+    for (int i = 0; i < n; ++i) out.outdeg[i] = int(count[i]);
+  } else {
+    // 16x16 block topology stored as CSR (same matrix as the block storage).
+    HostBSR b;
+    generate_bsr(c, b);
+    std::vector<long long> count(n, 0);
+    for (int i = 0; i < n; ++i) count[i] = b.outdeg[i];
+    finish_rows(out, count);
+    out.w16.assign(out.syn.size(), 0);
+    for (int bc = 0; bc < b.nb; ++bc)
+      for (int col = 0; col < 16; ++col) {
+        const int pre = bc * 16 + col;
+        long long e = out.row[pre];
+        for (long long k = b.bcol[bc]; k < b.bcol[bc + 1]; ++k) {
+          const int br = int(b.blk[k] & kPostMask);
+          const int d = int(b.blk[k] >> 28) + 1;
+          for (int r = 0; r < 16; ++r) {
+            const uint16_t hb = b.tiles[(size_t(k) * 16 + col) * 16 + r];
+            if ((hb & 0x7FFFu) == 0) continue;
+            out.syn[e] = pack_word(br * 16 + r, d);
+            out.w16[e] = hb;
+            ++e;
+            const double w = double(__half2float(__ushort_as_half(hb)));
+            (w < 0 ? sum_i : sum_e)[br * 16 + r] += std::fabs(w);
+          }
+        }
+        out.outdeg[pre] = int(count[pre]);
+      }
+  }
+  check_ring_bound(n, sum_e, sum_i);
+}
+
+// ---------------------------------------------------------------------------
+// 16x16 block generation: per block-row, `bsr_blocks` distinct block-columns
+// and, per block, `bsr_fill` distinct entries (Floyd's sampling), one delay
+// per block.  Stored by block-column, blocks in ascending block-row order.
+// ---------------------------------------------------------------------------
+namespace {
+// Floyd's algorithm: m distinct values of [0, range), keyed draws (a, salt+j).
+void floyd(const Stream &s, uint64_t a, uint64_t salt, int range, int m, std::vector<int> &out) {
+  out.clear();
+  for (int j = range - m; j < range; ++j) {
+    const int t = int(s.below(a, salt + uint64_t(j), uint64_t(j) + 1));
+    if (std::find(out.begin(), out.end(), t) == out.end()) out.push_back(t);
+    else out.push_back(j);
+  }
+  std::sort(out.begin(), out.end());
+}
+} // namespace
+
+void generate_bsr(const ng_net_config &c, HostBSR &out) {
+  const int n = c.n, NB = n / 16, M = c.bsr_blocks, F = c.bsr_fill;
+  out.nb = NB;
+  const WeightDraw wd(c);
+  const Stream blk(c.seed, S_BLOCK), fill(c.seed, S_FILL), dly(c.seed, S_DELAY);
+  const uint64_t dspan = uint64_t(c.delay_max - c.delay_min + 1);
+  // By block-row first.
+  std::vector<int> rcols(size_t(NB) * M);
+  std::vector<uint32_t> rmeta(size_t(NB) * M);
+  std::vector<uint16_t> rtiles(size_t(NB) * M * 256, 0);
+#pragma omp parallel
+  {
+    std::vector<int> cols, pos;
+#pragma omp for schedule(dynamic, 16)
+    for (int br = 0; br < NB; ++br) {
+      floyd(blk, uint64_t(br), 0, NB, M, cols);
+      for (int m = 0; m < M; ++m) {
+        const int bc = cols[m];
+        const size_t x = size_t(br) * M + m;
+        rcols[x] = bc;
+        rmeta[x] = pack_word(br, c.delay_min + int(dly.below(uint64_t(br), uint64_t(bc), dspan)));
+        floyd(fill, uint64_t(br), uint64_t(bc) * 256, 256, F, pos);
+        for (int p : pos) {
+          const int r = p / 16, col = p % 16; // entry (post row r, pre column col)
+          const int pre = bc * 16 + col;
+          uint16_t hb = 0;
+          wd.draw(uint64_t(br) * 16 + r, uint64_t(pre), pre >= c.n_exc, &hb);
+          rtiles[x * 256 + size_t(col) * 16 + r] = hb;
+        }
+      }
+    }
+  }
+  // Regroup by block-column (stable in block-row order).
+  out.bcol.assign(size_t(NB) + 1, 0);
+  for (size_t x = 0; x < rcols.size(); ++x) out.bcol[rcols[x] + 1]++;
+  for (int b = 0; b < NB; ++b) out.bcol[b + 1] += out.bcol[b];
+  const size_t nblk = rcols.size();
+  out.blk.assign(nblk, 0);
+  out.tiles.assign(nblk * 256, 0);
+  std::vector<long long> at(out.bcol.begin(), out.bcol.end() - 1);
+  std::vector<double> sum_e(n, 0.0), sum_i(n, 0.0);
+  out.outdeg.assign(n, 0);
+  for (size_t x = 0; x < nblk; ++x) {
+    const long long k = at[rcols[x]]++;
+    out.blk[k] = rmeta[x];
+    std::memcpy(&out.tiles[size_t(k) * 256], &rtiles[x * 256], 512);
+    const int br = int(rmeta[x] & kPostMask), bc = rcols[x];
+    for (int col = 0; col < 16; ++col)
+      for (int r = 0; r < 16; ++r) {
+        const uint16_t hb = rtiles[x * 256 + size_t(col) * 16 + r];
+        if ((hb & 0x7FFFu) == 0) continue;
+        out.outdeg[bc * 16 + col]++;
+        const double w = double(__half2float(__ushort_as_half(hb)));
+        (w < 0 ? sum_i : sum_e)[br * 16 + r] += std::fabs(w);
+      }
+  }
+  check_ring_bound(n, sum_e, sum_i);
+}
+
+void csr_from_edges(const ng_net_config &c, int64_t nnz, const int32_t *pre, const int32_t *post,
+                    const int32_t *delay, const float *w, HostCSR &out) {
+  const int n = c.n;
+  out.n = n;
+  if (nnz < 0 || (nnz > 0 && (!pre || !post || !delay || !w)))
+    throw std::invalid_argument("Null synapse arrays");
+  std::vector<long long> count(n, 0);
+  std::vector<double> sum_e(n, 0.0), sum_i(n, 0.0);
+  for (int64_t e = 0; e < nnz; ++e) {
+    if (pre[e] < 0 || pre[e] >= n || post[e] < 0 || post[e] >= n)
+      throw std::invalid_argument("Synapse endpoint out of range");
+    if (delay[e] < 1 || delay[e] > kRingSlots - 1) throw std::invalid_argument("Synapse delay must be in 1..15");
+    if (!std::isfinite(w[e])) throw std::invalid_argument("Non-finite synaptic weight");
+    const double q = double(std::fabs(w[e])) * 16777216.0;
+    if (q != std::floor(q)) throw std::invalid_argument("Weights must be multiples of 2^-24 nS");
+    if (w[e] == 0.f) continue;
+    ++count[pre[e]];
+    (w[e] < 0 ? sum_i : sum_e)[post[e]] += std::fabs(double(w[e]));
+  }
+  check_ring_bound(n, sum_e, sum_i);
+  finish_rows(out, count);
+  out.w32.assign(out.syn.size(), 0.f);
+  std::vector<long long> fill(out.row.begin(), out.row.end() - 1);
+  for (int64_t e = 0; e < nnz; ++e) {
+    if (w[e] == 0.f) continue;
+    const long long k = fill[pre[e]]++;
+    out.syn[k] = pack_word(post[e], delay[e]);
+    out.w32[k] = w[e];
+  }
+  for (int i = 0; i < n; ++i) out.outdeg[i] = int(count[i]);
+}
+
+// ---------------------------------------------------------------------------
+// Host topology objects.
+// ---------------------------------------------------------------------------
+int64_t Topology::synapses() const {
+  int64_t total = 0;
+  for (int x : blocks ? bsr.outdeg : csr.outdeg) total += x;
+  return total;
+}
+
+void Topology::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight) const {
+  size_t k = 0;
+  auto emit = [&](int p, int q, int d, float w) {
+    if (pre) pre[k] = p;
+    if (post) post[k] = q;
+    if (delay) delay[k] = d;
+    if (weight) weight[k] = w;
+    ++k;
+  };
+  if (blocks) {
+    for (int bc = 0; bc < bsr.nb; ++bc)
+      for (int col = 0; col < 16; ++col)
+        for (long long b = bsr.bcol[bc]; b < bsr.bcol[bc + 1]; ++b) {
+          const int br = int(bsr.blk[b] & kPostMask), d = int(bsr.blk[b] >> 28) + 1;
+          for (int r = 0; r < 16; ++r) {
+            const uint16_t hb = bsr.tiles[(size_t(b) * 16 + col) * 16 + r];
+            if ((hb & 0x7FFFu) == 0) continue;
+            emit(bc * 16 + col, br * 16 + r, d, __half2float(__ushort_as_half(hb)));
+          }
+        }
+    return;
+  }
+  const bool half = !csr.w16.empty();
+  for (int i = 0; i < csr.n; ++i)
+    for (long long e = csr.row[i]; e < csr.row[i + 1]; ++e) {
+      const float w = half ? __half2float(__ushort_as_half(csr.w16[e])) : csr.w32[e];
+      if (w != 0.f) emit(i, int(csr.syn[e] & kPostMask), int(csr.syn[e] >> 28) + 1, w);
+    }
+}
+
+Topology *make_topology(const ng_net_config &cfg) {
+  validate_config(cfg);
+  auto t = std::make_unique<Topology>();
+  t->cfg = cfg;
+  t->blocks = cfg.storage == 1;
+  if (t->blocks) generate_bsr(cfg, t->bsr);
+  else generate_csr(cfg, t->csr);
+  return t.release();
+}
+
+Topology *make_topology_edges(const ng_net_config &cfg, int64_t nnz, const int32_t *pre, const int32_t *post,
+                              const int32_t *delay, const float *w) {
+  ng_net_config c = cfg;
+  c.storage = 0;
+  c.topology = NG_TOPO_ERDOS_RENYI; // topology fields are unused for explicit edges
+  c.p_connect = 0.f;
+  c.weight_kind = NG_W_LOGNORMAL_F32;
+  validate_config(c);
+  auto t = std::make_unique<Topology>();
+  t->cfg = c;
+  csr_from_edges(c, nnz, pre, post, delay, w, t->csr);
+  return t.release();
+}
+
+// ---------------------------------------------------------------------------
+// Device network.
+// ---------------------------------------------------------------------------
+namespace {
+template <class T> DeviceBuffer upload_vec(const std::vector<T> &v) {
+  DeviceBuffer d(std::max<size_t>(v.size(), 1) * sizeof(T));
+  if (!v.empty()) NGB_CUDA(cudaMemcpy(d.as<void>(), v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return d;
+}
+float decay_of(float dt, float tau) { return float(std::exp(-double(dt) / double(tau))); }
+} // namespace
+
+Network::Network(const Topology &topo) : cfg(topo.cfg) {
+  const ng_net_config &c = topo.cfg;
+  const HostCSR *csr = topo.blocks ? nullptr : &topo.csr;
+  const HostBSR *bsr = topo.blocks ? &topo.bsr : nullptr;
+  device = require_sm100_device();
+  n_ = c.n;
+  NetDev &d = dev_;
+  d.n = n_;
+  d.n_exc = c.n_exc;
+  if (bsr) {
+    bcol_ = upload_vec(bsr->bcol);
+    blk_ = upload_vec(bsr->blk);
+    tiles_ = upload_vec(bsr->tiles);
+    outdeg_ = upload_vec(bsr->outdeg);
+    d.bsr = 1;
+    d.bcol = bcol_.as<long long>();
+    d.blk = blk_.as<uint32_t>();
+    d.tiles = tiles_.as<uint16_t>();
+    for (int x : bsr->outdeg) nnz_ += x;
+  } else {
+    row_ = upload_vec(csr->row);
+    syn_ = upload_vec(csr->syn);
+    outdeg_ = upload_vec(csr->outdeg);
+    if (!csr->w16.empty() || csr->w32.empty()) {
+      w_ = upload_vec(csr->w16.empty() ? std::vector<uint16_t>(csr->syn.size(), 0) : csr->w16);
+      d.w_half = 1;
+    } else {
+      w_ = upload_vec(csr->w32);
+      d.w_half = 0;
+    }
+    d.row = row_.as<long long>();
+    d.syn = syn_.as<uint32_t>();
+    d.w = w_.as<void>();
+    for (int x : csr->outdeg) nnz_ += x;
+  }
+  d.outdeg = outdeg_.as<int>();
+  const size_t N = size_t(n_);
+  v_.reset(N * 4);
+  a_.reset(N * 4);
+  ge_.reset(N * 4);
+  gi_.reset(N * 4);
+  ref_.reset(N * 4);
+  ring_.reset(size_t(kRingSlots) * N * 8);
+  std::vector<float> v0(N, c.e_leak_mv);
+  NGB_CUDA(cudaMemcpy(v_.as<float>(), v0.data(), N * 4, cudaMemcpyHostToDevice));
+  NGB_CUDA(cudaMemset(a_.as<float>(), 0, N * 4));
+  NGB_CUDA(cudaMemset(ge_.as<float>(), 0, N * 4));
+  NGB_CUDA(cudaMemset(gi_.as<float>(), 0, N * 4));
+  NGB_CUDA(cudaMemset(ref_.as<int>(), 0, N * 4));
+  NGB_CUDA(cudaMemset(ring_.as<int2>(), 0, size_t(kRingSlots) * N * 8));
+  d.v = v_.as<float>();
+  d.a = a_.as<float>();
+  d.ge = ge_.as<float>();
+  d.gi = gi_.as<float>();
+  d.ref = ref_.as<int>();
+  d.ring = ring_.as<int2>();
+  d.dE = decay_of(c.dt_ms, c.tau_exc_ms);
+  d.dI = decay_of(c.dt_ms, c.tau_inh_ms);
+  d.dA = decay_of(c.dt_ms, c.tau_adapt_ms);
+  d.g_leak = c.g_leak_ns;
+  d.gLEL = c.g_leak_ns * c.e_leak_mv;
+  d.e_inh = c.e_inh_mv;
+  d.v_th = c.v_thresh_mv;
+  d.v_reset = c.v_reset_mv;
+  d.cap_e = c.cap_exc_pf;
+  d.cap_i = c.cap_inh_pf;
+  d.neg_dt = -c.dt_ms;
+  d.adapt_inc = c.adapt_inc_pa;
+  d.bias = c.bias_pa;
+  d.drive_ns = c.drive_ns;
+  d.drive_kind = c.drive_kind;
+  const double thr = double(c.drive_p) * 4294967296.0;
+  d.drive_thr = thr >= 4294967295.0 ? 0xFFFFFFFFu : uint32_t(thr);
+  d.drive_key = mix64(c.seed ^ 0xD41Eull);
+  d.ref_ticks = int(std::lround(double(c.t_ref_ms) / double(c.dt_ms)));
+  NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+}
+
+Network::~Network() {
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void Network::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight) {
+  NGB_CUDA(cudaSetDevice(device));
+  Topology t;
+  t.cfg = cfg;
+  t.blocks = dev_.bsr != 0;
+  if (t.blocks) {
+    HostBSR &b = t.bsr;
+    b.nb = n_ / 16;
+    b.bcol.resize(size_t(b.nb) + 1);
+    NGB_CUDA(cudaMemcpy(b.bcol.data(), bcol_.as<void>(), b.bcol.size() * 8, cudaMemcpyDeviceToHost));
+    b.blk.resize(size_t(b.bcol[b.nb]));
+    b.tiles.resize(b.blk.size() * 256);
+    if (!b.blk.empty()) {
+      NGB_CUDA(cudaMemcpy(b.blk.data(), blk_.as<void>(), b.blk.size() * 4, cudaMemcpyDeviceToHost));
+      NGB_CUDA(cudaMemcpy(b.tiles.data(), tiles_.as<void>(), b.tiles.size() * 2, cudaMemcpyDeviceToHost));
+    }
+  } else {
+    HostCSR &h = t.csr;
+    h.n = n_;
+    h.row.resize(size_t(n_) + 1);
+    NGB_CUDA(cudaMemcpy(h.row.data(), row_.as<void>(), h.row.size() * 8, cudaMemcpyDeviceToHost));
+    const size_t total = size_t(h.row[n_]);
+    h.syn.resize(total);
+    if (total) NGB_CUDA(cudaMemcpy(h.syn.data(), syn_.as<void>(), total * 4, cudaMemcpyDeviceToHost));
+    if (dev_.w_half) {
+      h.w16.resize(total);
+      if (total) NGB_CUDA(cudaMemcpy(h.w16.data(), w_.as<void>(), total * 2, cudaMemcpyDeviceToHost));
+    } else {
+      h.w32.resize(total);
+      if (total) NGB_CUDA(cudaMemcpy(h.w32.data(), w_.as<void>(), total * 4, cudaMemcpyDeviceToHost));
+    }
+  }
+  t.export_edges(pre, post, delay, weight);
+}
+
+void Network::set_state(const float *v, const float *a, const float *ge, const float *gi, const int32_t *ref,
+                        const int32_t *ring, int64_t tick) {
+  NGB_CUDA(cudaSetDevice(device));
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  const size_t N = size_t(n_);
+  if (v) NGB_CUDA(cudaMemcpy(v_.as<void>(), v, N * 4, cudaMemcpyHostToDevice));
+  if (a) NGB_CUDA(cudaMemcpy(a_.as<void>(), a, N * 4, cudaMemcpyHostToDevice));
+  if (ge) NGB_CUDA(cudaMemcpy(ge_.as<void>(), ge, N * 4, cudaMemcpyHostToDevice));
+  if (gi) NGB_CUDA(cudaMemcpy(gi_.as<void>(), gi, N * 4, cudaMemcpyHostToDevice));
+  if (ref) NGB_CUDA(cudaMemcpy(ref_.as<void>(), ref, N * 4, cudaMemcpyHostToDevice));
+  if (ring) NGB_CUDA(cudaMemcpy(ring_.as<void>(), ring, size_t(kRingSlots) * N * 8, cudaMemcpyHostToDevice));
+  if (tick < 0) throw std::invalid_argument("tick must be non-negative");
+  tick_ = tick;
+}
+
+void Network::get_state(float *v, float *a, float *ge, float *gi, int32_t *ref, int32_t *ring, int64_t *tick) {
+  NGB_CUDA(cudaSetDevice(device));
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  const size_t N = size_t(n_);
+  if (v) NGB_CUDA(cudaMemcpy(v, v_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
+  if (a) NGB_CUDA(cudaMemcpy(a, a_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
+  if (ge) NGB_CUDA(cudaMemcpy(ge, ge_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
+  if (gi) NGB_CUDA(cudaMemcpy(gi, gi_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
+  if (ref) NGB_CUDA(cudaMemcpy(ref, ref_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
+  if (ring) NGB_CUDA(cudaMemcpy(ring, ring_.as<void>(), size_t(kRingSlots) * N * 8, cudaMemcpyDeviceToHost));
+  if (tick) *tick = tick_;
+}
+
+void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_counts, cudaStream_t st) {
+  if (ticks < 0) throw std::invalid_argument("ticks must be non-negative");
+  const size_t words = (size_t(n_) + 31) / 32;
+  if (d_counts) NGB_CUDA(cudaMemsetAsync(d_counts, 0, size_t(ticks) * 16, st));
+  for (int k = 0; k < ticks; ++k)
+    launch_net_tick(dev_, tick_ + k, d_spikes ? d_spikes + size_t(k) * words : nullptr,
+                    d_counts ? d_counts + 2 * size_t(k) : nullptr, st);
+  NGB_CUDA(cudaGetLastError());
+  tick_ += ticks;
+}
+
+void Network::run_host(int ticks, uint32_t *spikes, int64_t *counts) {
+  NGB_CUDA(cudaSetDevice(device));
+  const size_t words = (size_t(n_) + 31) / 32;
+  const int chunk = 1024;
+  if (spikes) rec_spikes_.reset(size_t(std::min(ticks, chunk)) * words * 4 + 4);
+  if (counts) rec_counts_.reset(size_t(std::min(ticks, chunk)) * 16 + 16);
+  for (int done = 0; done < ticks; done += chunk) {
+    const int k = std::min(chunk, ticks - done);
+    enqueue(k, spikes ? rec_spikes_.as<uint32_t>() : nullptr,
+            counts ? rec_counts_.as<unsigned long long>() : nullptr, stream);
+    if (spikes)
+      NGB_CUDA(cudaMemcpyAsync(spikes + size_t(done) * words, rec_spikes_.as<void>(), size_t(k) * words * 4,
+                               cudaMemcpyDeviceToHost, stream));
+    if (counts)
+      NGB_CUDA(cudaMemcpyAsync(counts + 2 * size_t(done), rec_counts_.as<void>(), size_t(k) * 16,
+                               cudaMemcpyDeviceToHost, stream));
+    NGB_CUDA(cudaStreamSynchronize(stream));
+  }
+  NGB_CUDA(cudaStreamSynchronize(stream));
+}
+
+} // namespace ngb

@@ -1,0 +1,86 @@
+// Host side of the isolated-tick spiking network: topology generation, device
+// layout (CSR or 16x16 blocks by presynaptic neuron), state and tick loop.
+#pragma once
+#include "common.h"
+#include "net_kernels.h"
+#include "neurogen_b200.h"
+
+#include <cstdint>
+#include <mutex>
+#include <vector>
+
+namespace ngb {
+
+// Synapses by presynaptic neuron, host form.
+struct HostCSR {
+  int n = 0;
+  std::vector<long long> row;    // [n+1], rows padded to multiples of 8
+  std::vector<uint32_t> syn;     // post | (delay-1) << 28
+  std::vector<float> w32;        // signed weights (fp32 storage), or
+  std::vector<uint16_t> w16;     // fp16 bits (fp16 storage)
+  std::vector<int> outdeg;       // non-zero synapses per row
+};
+
+// 16x16 blocks by block-column, host form.
+struct HostBSR {
+  int nb = 0;                    // block-columns (= block-rows)
+  std::vector<long long> bcol;   // [nb+1]
+  std::vector<uint32_t> blk;     // block-row | (delay-1) << 28
+  std::vector<uint16_t> tiles;   // fp16 [block][16 columns][16 rows]
+  std::vector<int> outdeg;       // non-zero synapses per presynaptic neuron
+};
+
+// A generated or caller-given synapse set on the host (no device needed).
+struct Topology {
+  ng_net_config cfg;
+  bool blocks = false; // true: `bsr` holds the synapses, else `csr`
+  HostCSR csr;
+  HostBSR bsr;
+  int64_t synapses() const;
+  // Synapse list, presynaptic-major (arrays of synapses() entries; any may be null).
+  void export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight) const;
+};
+Topology *make_topology(const ng_net_config &cfg);
+Topology *make_topology_edges(const ng_net_config &cfg, int64_t nnz, const int32_t *pre, const int32_t *post,
+                              const int32_t *delay, const float *w);
+
+// Deterministic generators (same seed -> same network on any machine).
+void generate_csr(const ng_net_config &c, HostCSR &out);
+void generate_bsr(const ng_net_config &c, HostBSR &out);
+void csr_from_edges(const ng_net_config &c, int64_t nnz, const int32_t *pre, const int32_t *post,
+                    const int32_t *delay, const float *w, HostCSR &out);
+void validate_config(const ng_net_config &c);
+
+class Network {
+public:
+  explicit Network(const Topology &topo);
+  ~Network();
+  Network(const Network &) = delete;
+  Network &operator=(const Network &) = delete;
+
+  int64_t synapses() const { return nnz_; }
+  void export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight);
+  void set_state(const float *v, const float *a, const float *ge, const float *gi, const int32_t *ref,
+                 const int32_t *ring, int64_t tick);
+  void get_state(float *v, float *a, float *ge, float *gi, int32_t *ref, int32_t *ring, int64_t *tick);
+  // Enqueue `ticks` ticks on `st`; d_spikes [ticks][words] and d_counts
+  // [ticks][2] (u64) are optional device outputs.
+  void enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_counts, cudaStream_t st);
+  void run_host(int ticks, uint32_t *spikes, int64_t *counts);
+
+  ng_net_config cfg;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mutex;
+
+private:
+  int n_ = 0;
+  int64_t nnz_ = 0;
+  long long tick_ = 0;
+  NetDev dev_{};
+  DeviceBuffer row_, syn_, w_, outdeg_, bcol_, blk_, tiles_;
+  DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
+  DeviceBuffer rec_spikes_, rec_counts_;
+};
+
+} // namespace ngb

@@ -1,0 +1,47 @@
+// Launch interface of the isolated-tick network kernels (net_kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ngb {
+
+constexpr int kRingSlots = 16; // delay ring depth; delays 1..15 ticks
+constexpr float kRingQuantum = 5.9604644775390625e-08f; // 2^-24 nS per ring unit
+
+// Synapse word: postsynaptic index in bits 0-27, (delay - 1) in bits 28-31.
+constexpr uint32_t kPostMask = 0x0FFFFFFFu;
+
+struct NetDev {
+  int n, n_exc;
+  // CSR by presynaptic neuron, rows padded to multiples of 8 with zero weights.
+  const long long *row; // [n+1]
+  const uint32_t *syn;  // packed post/delay
+  const void *w;        // fp16 or fp32 signed weights (nS; negative = inhibitory)
+  int w_half;
+  const int *outdeg; // non-zero synapses per presynaptic neuron
+  // 16x16 block storage by block-column (pre block), blocks sorted by block-row.
+  int bsr;
+  const long long *bcol; // [n/16+1]
+  const uint32_t *blk;   // block-row | (delay-1) << 28
+  const uint16_t *tiles; // fp16 [block][16 pre columns][16 post rows]
+  // State (fp32 SoA) and the E/I delay ring [16][n] of int2 (E, I) in 2^-24 nS.
+  float *v, *a, *ge, *gi;
+  int *ref;
+  int2 *ring;
+  // Constants (see net_kernels.cu for the exact operation order).
+  float dE, dI, dA, g_leak, gLEL, e_inh, v_th, v_reset, cap_e, cap_i, neg_dt, adapt_inc, bias,
+      drive_ns;
+  int drive_kind; // 0 conductance events, 1 imposed spikes
+  uint32_t drive_thr;
+  unsigned long long drive_key;
+  int ref_ticks;
+};
+
+// One tick t: ALIF update of every neuron, spike bitmask by warp ballot,
+// push of every spiking neuron's synapses into ring slots (t + d) % 16.
+// spikes_out: this tick's ceil(n/32) bit words or null.  counts: [2] u64
+// accumulators (spikes, synaptic events) or null.
+void launch_net_tick(const NetDev &d, long long t, uint32_t *spikes_out,
+                     unsigned long long *counts, cudaStream_t s);
+
+} // namespace ngb

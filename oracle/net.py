@@ -1,0 +1,109 @@
+"""ORACLE (test infrastructure only): ctypes access to oracle/net_oracle.c.
+
+``NetOracle`` runs the conductance ALIF network with per-synapse delays on the CPU, in the
+fp32 arithmetic contract of the CUDA engine (bit-exact target) or in fp64 (pinned to the
+reference's neurogen/biology.py).  Only tests/, ``__graft_entry__.smoke()`` and bench.py's
+CPU-baseline leg use this module.
+"""
+import ctypes as ct
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+RING = 16
+
+
+class Params(ct.Structure):
+    _fields_ = [('n', ct.c_int32), ('n_exc', ct.c_int32), ('dt', ct.c_float), ('cap_e', ct.c_float),
+                ('cap_i', ct.c_float), ('g_leak', ct.c_float), ('e_leak', ct.c_float),
+                ('e_inh', ct.c_float), ('v_th', ct.c_float), ('v_reset', ct.c_float),
+                ('t_ref', ct.c_float), ('tau_e', ct.c_float), ('tau_i', ct.c_float),
+                ('tau_a', ct.c_float), ('adapt_inc', ct.c_float), ('bias', ct.c_float),
+                ('drive_kind', ct.c_int32), ('drive_p', ct.c_float), ('drive_ns', ct.c_float),
+                ('seed', ct.c_uint64)]
+
+
+def params_from(cfg):
+    """Oracle parameters from an ng_net_config (ctypes struct) or a dict of the same names."""
+    g = (lambda k: getattr(cfg, k)) if not isinstance(cfg, dict) else cfg.__getitem__
+    return Params(g('n'), g('n_exc'), g('dt_ms'), g('cap_exc_pf'), g('cap_inh_pf'), g('g_leak_ns'),
+                  g('e_leak_mv'), g('e_inh_mv'), g('v_thresh_mv'), g('v_reset_mv'), g('t_ref_ms'),
+                  g('tau_exc_ms'), g('tau_inh_ms'), g('tau_adapt_ms'), g('adapt_inc_pa'),
+                  g('bias_pa'), g('drive_kind'), g('drive_p'), g('drive_ns'), g('seed'))
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ct.c_void_p)
+
+
+class NetOracle:
+    def __init__(self, cfg, pre, post, delay, weight):
+        lib = self.lib = ct.CDLL(str(HERE / 'liboracle.so'))
+        lib.on_create.restype = ct.c_void_p
+        lib.on_create.argtypes = [ct.POINTER(Params), ct.c_int64] + [ct.c_void_p] * 4
+        lib.on_destroy.argtypes = [ct.c_void_p]
+        lib.on_run.argtypes = [ct.c_void_p, ct.c_int, ct.c_void_p, ct.c_void_p]
+        lib.on_run_mt.argtypes = [ct.c_void_p, ct.c_int, ct.c_void_p]
+        lib.on_run64.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 5
+        lib.on_set_state.argtypes = [ct.c_void_p] + [ct.c_void_p] * 6 + [ct.c_int64]
+        lib.on_get_state.argtypes = [ct.c_void_p] + [ct.c_void_p] * 7
+        lib.on_set_state64.argtypes = [ct.c_void_p] + [ct.c_void_p] * 5
+        self.params = params_from(cfg)
+        self.n = self.params.n
+        self.words = (self.n + 31) // 32
+        self._keep = [np.ascontiguousarray(x, dt) for x, dt in
+                      ((pre, np.int32), (post, np.int32), (delay, np.int32), (weight, np.float64))]
+        self.h = lib.on_create(ct.byref(self.params), len(self._keep[0]), *[_p(x) for x in self._keep])
+
+    def __del__(self):
+        if getattr(self, 'h', None):
+            self.lib.on_destroy(self.h)
+
+    def run(self, ticks):
+        """fp32 contract -> (spike words uint32 [ticks, words], counts int64 [ticks, 2])."""
+        spikes = np.zeros((ticks, self.words), np.uint32)
+        counts = np.zeros((ticks, 2), np.int64)
+        self.lib.on_run(self.h, ticks, _p(spikes), _p(counts))
+        return spikes, counts
+
+    def run_mt(self, ticks):
+        """on_run on all OpenMP threads (identical results) -> counts int64 [ticks, 2]."""
+        counts = np.zeros((ticks, 2), np.int64)
+        self.lib.on_run_mt(self.h, ticks, _p(counts))
+        return counts
+
+    def run64(self, ticks, current=None):
+        """fp64 equations -> (spike words, v [ticks, n], ge, gi)."""
+        spikes = np.zeros((ticks, self.words), np.uint32)
+        v = np.zeros((ticks, self.n))
+        ge = np.zeros((ticks, self.n))
+        gi = np.zeros((ticks, self.n))
+        cur = None if current is None else np.ascontiguousarray(current, np.float64)
+        self.lib.on_run64(self.h, ticks, _p(cur), _p(spikes), _p(v), _p(ge), _p(gi))
+        return spikes, v, ge, gi
+
+    def set_state(self, v=None, a=None, ge=None, gi=None, ref=None, ring=None, tick=0):
+        arrs = [None if x is None else np.ascontiguousarray(x, dt) for x, dt in
+                ((v, np.float32), (a, np.float32), (ge, np.float32), (gi, np.float32),
+                 (ref, np.int32), (ring, np.int32))]
+        self.lib.on_set_state(self.h, *[_p(x) for x in arrs], tick)
+
+    def set_state64(self, v=None, a=None, ge=None, gi=None, ref=None):
+        arrs = [None if x is None else np.ascontiguousarray(x, np.float64) for x in (v, a, ge, gi, ref)]
+        self.lib.on_set_state64(self.h, *[_p(x) for x in arrs])
+
+    def get_state(self):
+        n = self.n
+        v, a, ge, gi = (np.zeros(n, np.float32) for _ in range(4))
+        ref = np.zeros(n, np.int32)
+        ring = np.zeros((RING, n, 2), np.int32)
+        tick = np.zeros(1, np.int64)
+        self.lib.on_get_state(self.h, _p(v), _p(a), _p(ge), _p(gi), _p(ref), _p(ring), _p(tick))
+        return dict(v=v, a=a, ge=ge, gi=gi, ref=ref, ring=ring, tick=int(tick[0]))
+
+
+def unpack_spikes(words, n):
+    """uint32 words [..., ceil(n/32)] -> bool [..., n] (bit i%32 of word i/32)."""
+    bits = np.unpackbits(words.view(np.uint8), axis=-1, bitorder='little')
+    return bits[..., :n].astype(bool)

@@ -1,0 +1,223 @@
+"""GPU parity of the language core against the reference's own native CPU library.
+
+Bars (north star): spike indices identical for the first 100 ticks; state within 1e-5
+relative; logits within 1e-4 relative.  The engine reproduces the reference's fp32 operation
+order, so most outputs are bit-identical; the measured counts are printed for the record.
+"""
+import threading
+
+import numpy as np
+import pytest
+
+from neurogen_b200.language import LanguageConfig, NativeEngine, init_packed_weights
+from oracle.lang import OracleEngine, RefEngine
+
+pytestmark = pytest.mark.gpu
+
+SMALL = LanguageConfig(columns=3, width=17, regions=2, ticks=3, idle_steps=1, speech_width=16, mel_bins=8)
+STATE_RTOL, STATE_ATOL = 1e-5, 1e-6
+LOGIT_RTOL, LOGIT_ATOL = 1e-4, 1e-6
+
+
+def fields(cfg, state):
+    n, w = cfg.columns * 64, cfg.width
+    rs = 5 * n + w
+    out = {}
+    for r in range(cfg.regions):
+        b = state[..., r * rs:(r + 1) * rs]
+        out[r] = dict(v=b[..., :n], trace=b[..., n:2 * n], adapt=b[..., 2 * n:3 * n],
+                      last=b[..., 3 * n:4 * n], mem=b[..., 4 * n:4 * n + w], counts=b[..., 4 * n + w:])
+    return out
+
+
+def assert_state_close(cfg, got, want):
+    fg, fw = fields(cfg, got), fields(cfg, want)
+    for r in fg:
+        np.testing.assert_array_equal(fg[r]['last'], fw[r]['last'])     # spikes: exact
+        np.testing.assert_array_equal(fg[r]['counts'], fw[r]['counts'])
+        for k in ('v', 'trace', 'adapt', 'mem'):
+            np.testing.assert_allclose(fg[r][k], fw[r][k], rtol=STATE_RTOL, atol=STATE_ATOL, err_msg=k)
+
+
+def test_small_config_tokens_and_idle_vs_reference(golden_lang):
+    g = golden_lang
+    w = g['small_weights']
+    eng, ref = NativeEngine(SMALL, w), RefEngine(SMALL, w)
+    sa = np.zeros((1, ref.S), np.float32)
+    sb = sa[0].copy()
+    exact = total = 0
+    for tok in g['small_tokens']:
+        la, sa, aa, ha = eng.step_batch(np.array([tok]), sa)
+        lb, sb, ab, hb = ref.step(int(tok), sb)
+        np.testing.assert_allclose(la[0], lb, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+        assert_state_close(SMALL, sa[0], sb)
+        np.testing.assert_allclose(ha[0], hb, rtol=1e-4, atol=1e-6)
+        assert abs(aa[0] - ab) < 1e-7
+        exact += int(np.array_equal(sa[0], sb) and np.array_equal(la[0], lb))
+        total += 1
+    x = np.zeros((1, SMALL.width), np.float32)
+    for _ in range(8):
+        ha, sa, aa = eng.advance_batch(x, sa, idle=True)
+        hb, sb, ab = ref.advance(x[0], sb, True)
+        assert_state_close(SMALL, sa[0], sb)
+    print(f'bit-identical token steps: {exact}/{total}')
+
+
+def test_batch_rows_equal_single_session_runs():
+    cfg = LanguageConfig(columns=4, width=40, regions=2, ticks=2, idle_steps=1)
+    w = init_packed_weights(cfg, seed=3)
+    eng = NativeEngine(cfg, w)
+    B = 37  # exercises the tiled projection with a ragged session tile
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, 264, (6, B))
+    sb = np.zeros((B, eng.state_size), np.float32)
+    singles = [np.zeros((1, eng.state_size), np.float32) for _ in range(B)]
+    for t in range(6):
+        lb, sb, ab, hb = eng.step_batch(toks[t], sb)
+        for b in (0, 1, 17, 36):
+            l1, singles[b], a1, h1 = eng.step_batch(toks[t, b:b + 1], singles[b])
+            assert np.array_equal(l1[0], lb[b]) and np.array_equal(singles[b][0], sb[b])
+
+
+def recover_tick_spikes(cfg, before, after):
+    """Per-tick spikes of one advance with ticks=2: tick 1 is last_spikes, tick 0 follows from
+    the exact integer spike counters (counts_after - counts_before - tick1)."""
+    fb, fa = fields(cfg, before), fields(cfg, after)
+    out = []
+    for r in range(cfg.regions):
+        t1 = fa[r]['last']
+        t0 = fa[r]['counts'] - fb[r]['counts'] - t1
+        out.append(np.stack([t0, t1]))
+    return np.stack(out)  # [R, 2, n]
+
+
+def test_bc250_every_spike_of_first_128_ticks(golden_lang):
+    """Seed-0 BC-250 profile, free-running on the tokens of the benchmark stream: the spikes of
+    every unit at every tick of the first 32 tokens (64 advances x 2 ticks = 128 ticks per
+    region, 4 regions) equal the reference's."""
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng, orc = NativeEngine(cfg, w), OracleEngine(cfg, w)
+    emb = w[:264 * cfg.width].reshape(264, cfg.width)
+    zero = np.zeros((1, cfg.width), np.float32)
+    sg = np.zeros((1, orc.S), np.float32)
+    so = sg[0].copy()
+    for tok in golden_lang['bc250_tokens'][:32]:
+        lo, nxt, ao, ho, spikes = orc.step(int(tok), so, record=True)
+        per = spikes.reshape(2, cfg.regions, cfg.ticks, orc.n)
+        h0, s1, _ = eng.advance_batch(emb[tok][None], sg, idle=False)
+        np.testing.assert_array_equal(recover_tick_spikes(cfg, sg[0], s1[0]), per[0])
+        h1, s2, _ = eng.advance_batch(zero, s1, idle=True)
+        np.testing.assert_array_equal(recover_tick_spikes(cfg, s1[0], s2[0]), per[1])
+        assert_state_close(cfg, s2[0], nxt)
+        sg, so = s2, nxt
+
+
+def test_bc250_token_step_teacher_forced_512_tokens(golden_lang):
+    """All 512 tokens of the seed-0 stream, each step started from the reference's own state:
+    logits 1e-4 relative, state 1e-5 relative, spikes exact (any spike decision within the fp32
+    noise of its threshold would be reported here)."""
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng, ref = NativeEngine(cfg, w), RefEngine(cfg, w)
+    s = np.zeros(ref.S, np.float32)
+    identical = 0
+    toks = golden_lang['bc250_tokens']
+    for i, tok in enumerate(toks):
+        lg, sg, ag, hg = eng.step_batch(np.array([tok]), s[None])
+        lr, sr, ar, hr = ref.step(int(tok), s)
+        if i < len(golden_lang['bc250_native_logits']):
+            assert np.array_equal(lr, golden_lang['bc250_native_logits'][i])
+        np.testing.assert_allclose(lg[0], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+        assert_state_close(cfg, sg[0], sr)
+        identical += int(np.array_equal(sg[0], sr) and np.array_equal(lg[0], lr))
+        s = sr
+    print(f'bit-identical BC-250 token steps: {identical}/{len(toks)}')
+
+
+def test_batched_sessions_vs_reference():
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng, ref = NativeEngine(cfg, w), RefEngine(cfg, w)
+    B = 6
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 264, (4, B))
+    sb = np.zeros((B, ref.S), np.float32)
+    sr = [np.zeros(ref.S, np.float32) for _ in range(B)]
+    for t in range(4):
+        lb, sb, ab, hb = eng.step_batch(toks[t], sb)
+        for b in range(B):
+            lr, sr[b], ar, hr = ref.step(int(toks[t, b]), sr[b])
+            np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+            assert_state_close(cfg, sb[b], sr[b])
+
+
+def test_errors_and_caller_state_immutability():
+    cfg = LanguageConfig(columns=2, width=8, regions=2, ticks=3, idle_steps=1)
+    eng = NativeEngine(cfg, init_packed_weights(cfg, seed=1))
+    s = np.zeros((1, eng.state_size), np.float32)
+    s[0, 3] = np.nan
+    with pytest.raises(ValueError, match='Non-finite native state'):
+        eng.step_batch(np.array([1]), s)
+    s[0, 3] = 0
+    with pytest.raises(ValueError, match='Token must be in 0..263'):
+        eng.step_batch(np.array([264]), s)
+    before = s.copy()
+    eng.step_batch(np.array([5]), s)
+    assert np.array_equal(before, s)
+    lib = eng.lib
+    bad = np.zeros(eng.state_size + 1, np.float32)
+    out = np.zeros(eng.state_size + 1, np.float32)
+    l = np.zeros(264, np.float32)
+    h = np.zeros(cfg.width, np.float32)
+    a = np.zeros(1, np.float32)
+    assert lib.ng_step(eng.handle, 1, bad, bad.size, out, l, h, a) == -1
+    assert lib.ng_error().decode() == 'Invalid native state size'
+
+
+def test_shared_handle_from_two_threads():
+    cfg = LanguageConfig(columns=2, width=16, regions=2, ticks=2, idle_steps=1)
+    eng = NativeEngine(cfg, init_packed_weights(cfg, seed=4))
+
+    def run(token):
+        s = np.zeros((1, eng.state_size), np.float32)
+        outs = []
+        for t in (257, token, token):
+            lg, s, _, _ = eng.step_batch(np.array([t]), s)
+            outs.append(lg.copy())
+        return outs
+
+    expected = [run(10), run(20)]
+    results = [None, None]
+
+    def worker(k, tok):
+        results[k] = run(tok)
+
+    threads = [threading.Thread(target=worker, args=(k, t)) for k, t in enumerate((10, 20))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    for e, r in zip(expected, results):
+        for x, y in zip(e, r):
+            assert np.array_equal(x, y)
+
+
+def test_pool_matches_host_batch():
+    cfg = LanguageConfig(columns=3, width=24, regions=2, ticks=2, idle_steps=1)
+    w = init_packed_weights(cfg, seed=6)
+    eng = NativeEngine(cfg, w)
+    lib = eng.lib
+    B = 5
+    pool = lib.ng_pool_create(eng.handle, B)
+    assert pool
+    try:
+        toks = np.array([1, 2, 3, 4, 5], np.int32)
+        logits = np.zeros((B, 264), np.float32)
+        assert lib.ng_pool_step(pool, toks, logits.ctypes.data, None, None) == 0
+        st = np.zeros((B, eng.state_size), np.float32)
+        assert lib.ng_pool_store(pool, st) == 0
+        lb, sb, _, _ = eng.step_batch(toks, np.zeros((B, eng.state_size), np.float32))
+        assert np.array_equal(lb, logits) and np.array_equal(sb, st)
+    finally:
+        lib.ng_pool_destroy(pool)

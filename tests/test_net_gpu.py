@@ -1,0 +1,143 @@
+"""GPU parity of the isolated-tick network engine against the fp32 oracle.
+
+The engine's contract is bit-exactness with oracle/net_oracle.c in its fp32 mode: every spike
+of every tick, and the full state (V, adaptation, g_E, g_I, refractory, delay ring) after the
+run.  Covered: Erdos-Renyi 8,192 (conductance drive, self-generated spikes), fixed fan-in and
+16x16 block matrices with fp16 weights (imposed spikes), CSR and block storage of the same
+block matrix, empty networks, explicit edge lists, the biology.py known-answer tests, and the
+full N=262,144 configuration through size-independent properties.
+"""
+import numpy as np
+import pytest
+
+from neurogen_b200.network import Network, Topology, default_config, isolated_8k, scaled_262k
+from oracle.net import NetOracle, unpack_spikes
+
+pytestmark = pytest.mark.gpu
+
+
+def run_both(cfg, ticks, state=None):
+    topo = Topology(cfg)
+    edges = topo.export()
+    net = topo.network()
+    orc = NetOracle(cfg, *edges)
+    if state:
+        net.set_state(**state)
+        orc.set_state(**state)
+    gs, gc = net.run(ticks)
+    os_, oc = orc.run(ticks)
+    return net, orc, (gs, gc), (os_, oc)
+
+
+def assert_same_state(net, orc):
+    a, b = net.get_state(), orc.get_state()
+    for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
+        assert np.array_equal(a[k], b[k]), k
+    assert a['tick'] == b['tick']
+
+
+def test_isolated_8k_bit_exact_200_ticks():
+    cfg = isolated_8k()
+    net, orc, (gs, gc), (os_, oc) = run_both(cfg, 200)
+    assert oc[:, 0].sum() > 1000
+    np.testing.assert_array_equal(gs, os_)  # every spike of every tick
+    np.testing.assert_array_equal(gc, oc)   # spikes and synaptic events per tick
+    assert_same_state(net, orc)
+
+
+@pytest.mark.parametrize('storage', ['csr', 'bsr'])
+def test_block_matrix_both_storages_bit_exact(storage):
+    cfg = default_config(n=4096, n_exc=3277, topology='bsr16', bsr_blocks=32, bsr_fill=64,
+                         weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, storage=storage,
+                         drive_kind='imposed', drive_p=0.03, seed=4)
+    net, orc, (gs, gc), (os_, oc) = run_both(cfg, 60)
+    np.testing.assert_array_equal(gs, os_)
+    np.testing.assert_array_equal(gc, oc)
+    assert_same_state(net, orc)
+
+
+def test_fixed_fanin_fp16_imposed_bit_exact():
+    cfg = default_config(n=16384, n_exc=13107, topology='fixed_fanin', fanin=128, weight_kind='halfnormal_f16',
+                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8)
+    net, orc, (gs, gc), (os_, oc) = run_both(cfg, 40)
+    np.testing.assert_array_equal(gs, os_)
+    np.testing.assert_array_equal(gc, oc)
+    assert_same_state(net, orc)
+
+
+def test_ragged_sizes_and_empty_network():
+    # n not a multiple of 32 (partial last warp) and an empty synapse set.
+    cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3)
+    net, orc, (gs, gc), (os_, oc) = run_both(cfg, 50)
+    np.testing.assert_array_equal(gs, os_)
+    assert_same_state(net, orc)
+    cfg0 = default_config(n=37, n_exc=30, p_connect=0.0, drive_ns=30.0, drive_p=0.2, seed=1)
+    net, orc, (gs, gc), (os_, oc) = run_both(cfg0, 20)
+    assert Topology(cfg0).synapses == 0
+    np.testing.assert_array_equal(gs, os_)
+    assert_same_state(net, orc)
+
+
+@pytest.mark.parametrize('excitatory', [True, False])
+def test_delayed_transmission_known_answer(excitatory):
+    cfg = default_config(n=4, n_exc=2, drive_p=0.0)
+    pre = 0 if excitatory else 2
+    w = 2.0 if excitatory else -2.0
+    net = Network(cfg, edges=([pre], [1], [3], [w]))
+    v = np.full(4, -65.0, np.float32)
+    v[pre] = 0.0
+    net.set_state(v=v)
+    spikes, counts = net.run(3)
+    assert unpack_spikes(spikes, 4)[0, pre] and counts[0, 1] == 1
+    st = net.get_state()
+    assert st['ge'].sum() == 0 and st['gi'].sum() == 0
+    net.run(1)
+    st = net.get_state()
+    assert (st['ge'][1] if excitatory else st['gi'][1]) == 2.0
+
+
+def test_passive_membrane_known_answer():
+    for dt in (.25, .5, 1.):
+        cfg = default_config(n=8, n_exc=6, drive_p=0.0, dt_ms=dt, bias_pa=100.0)
+        net = Network(cfg, edges=([], [], [], []))
+        net.run(round(10 / dt), record=False)
+        np.testing.assert_allclose(net.get_state()['v'][:6], -55 - 10 * np.exp(-10 / 20), atol=2e-4)
+
+
+def test_state_roundtrip_and_resume():
+    cfg = isolated_8k(seed=2)
+    topo = Topology(cfg)
+    a, b = topo.network(), topo.network()
+    a.run(30)
+    st = a.get_state()
+    b.set_state(**{k: st[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')}, tick=st['tick'])
+    sa, _ = a.run(40)
+    sb, _ = b.run(40)
+    np.testing.assert_array_equal(sa, sb)
+
+
+def test_scaled_262k_csr_properties():
+    """Full-size configuration: spike counts follow Bernoulli(p), every synaptic event is
+    delivered (ring mass conservation), and the first ticks are bit-exact with the oracle."""
+    cfg = scaled_262k('csr', rate=0.03)
+    topo = Topology(cfg)
+    edges = topo.export()
+    net = topo.network()
+    orc = NetOracle(cfg, *edges)
+    gs, gc = net.run(6)
+    os_, oc = orc.run(6)
+    np.testing.assert_array_equal(gs, os_)
+    np.testing.assert_array_equal(gc, oc)
+    assert_same_state(net, orc)
+    p = gc[:, 0] / cfg.n
+    assert np.all(np.abs(p - 0.03) < 5 * np.sqrt(0.03 * 0.97 / cfg.n))
+    # Mass conservation: after a run, the ring holds exactly the fixed-point sum of every
+    # weight emitted and not yet delivered.
+    fired = unpack_spikes(gs, cfg.n)
+    pre, post, delay, w = edges
+    q = np.round(np.abs(w.astype(np.float64)) * 2 ** 24).astype(np.int64)
+    pending = 0
+    for k in range(6):
+        sel = fired[k][pre] & (k + delay >= 6)
+        pending += q[sel].sum()
+    assert net.get_state()['ring'].astype(np.int64).sum() == pending
