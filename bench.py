@@ -50,6 +50,7 @@ def parse():
     p.add_argument('--rate', type=float, default=0.03)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--ticks', type=int, default=0, help='override ticks per step (profiling runs)')
     return p.parse_args()
 
 
@@ -186,30 +187,30 @@ def bench_ticks(args, dist):
     from neurogen_b200.network import Topology
     lib = library()
     cfg, ticks, wl = tick_config(args.workload, args.rate)
+    ticks = args.ticks or ticks
     cfg.seed = cfg.seed + dist.rank  # independent replica per rank
     t0 = time.time()
     topo = Topology(cfg)
     net = topo.network()
     setup_s = time.time() - t0
+    split = cfg.launch == 2 or (cfg.launch == 0 and cfg.n >= 65536)
     stream = torch.cuda.current_stream()
-    counts = torch.zeros((ticks, 2), dtype=torch.int64, device='cuda')
 
     def step():
-        if lib.ng_net_run_device(net.h, ticks, None, counts.data_ptr(), stream.cuda_stream):
+        if lib.ng_net_run_device(net.h, ticks, None, None, stream.cuda_stream):
             raise RuntimeError(lib.ng_error().decode())
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
-    spikes = events = 0
+    s0, e0 = net.stats()
     with Clocks(torch.cuda.current_device()) as clk:
         elapsed = 0.0
         for _ in range(args.steps):
             elapsed += cuda_timer(step, stream)
-            c = counts.cpu().numpy()
-            spikes += int(c[:, 0].sum())
-            events += int(c[:, 1].sum())
+    s1, e1 = net.stats()
+    spikes, events = s1 - s0, e1 - e0
     dist.barrier()
     t_max = dist.max(elapsed)
     total_ticks = ticks * args.steps
@@ -233,7 +234,7 @@ def bench_ticks(args, dist):
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
                      'frac': achieved / pk['hbm_gbs'], 'traffic': None,
                      'bytes_per_launch': b_tick, 'kernel': 'k_net_tick', 'peak_source': src},
-        'gpu_launches': total_ticks,
+        'gpu_launches': total_ticks * (2 if split else 1) + args.steps * (-(-ticks // 64) + 1),
         'clocks': clk.summary(),
     }
     if not args.no_e2e:
@@ -335,7 +336,7 @@ def lang_launches_per_token(cfg):
         for r in range(cfg.regions):
             sensory = adv == 0 or r > 0
             per += int(sensory) + cfg.ticks + (cfg.ticks % 2) + 2  # input, ticks, copy, output, norm
-    return per + 1  # head
+    return per + 2  # head, activity
 
 
 def bench_lang(args, dist):

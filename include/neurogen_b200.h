@@ -147,7 +147,9 @@ typedef struct {
   float drive_p;                /* Bernoulli probability per neuron per tick */
   float drive_ns;               /* conductance added per drive event */
   int32_t storage;              /* 0 = CSR push, 1 = BSR push (BSR16 topology) */
-  int32_t reserved[7];
+  int32_t launch;               /* 0 = auto, 1 = one fused launch per tick,
+                                   2 = split membrane / push launches            */
+  int32_t reserved[6];
 } ng_net_config;
 
 /* Fill `cfg` with the biology.py defaults (BiologyConfig, biology.py:19-77;
@@ -196,6 +198,10 @@ int ng_net_get_state(void *net, float *v, float *adapt, float *g_exc,
  * uint32 bitmask words, bit (i % 32) of word i/32 = neuron i spiked.
  * counts (host, may be NULL): [ticks] spikes per tick. */
 int ng_net_run(void *net, int ticks, uint32_t *spikes, int64_t *counts);
+
+/* Running totals since creation: totals[0] = spikes, totals[1] = synaptic
+ * events delivered (host array of 2).  Synchronises the network's stream. */
+int ng_net_stats(void *net, int64_t *totals);
 
 /* Device-side run on a caller stream (NULL = the network's stream): no host
  * copies, no synchronisation.  d_spikes/d_counts may be NULL. */

@@ -31,9 +31,34 @@ struct Pool {
   DeviceBuffer state, tokens, logits, hidden, act;
   Scratch sc;
   cudaStream_t stream = nullptr;
+  cudaGraphExec_t graph = nullptr; // one token step of the whole pool
   std::mutex mu;
   ~Pool() {
+    if (graph) cudaGraphExecDestroy(graph);
     if (stream) cudaStreamDestroy(stream);
+  }
+  // Enqueue one token step reading `tokens` and writing logits/hidden/act
+  // into the pool's own buffers.  The step is captured into a CUDA graph on
+  // first use and replayed afterwards (its buffers never move).
+  void token_step(cudaStream_t st) {
+    if (!graph) {
+      const DeviceModel &m = engine->device();
+      cudaGraph_t g = nullptr;
+      NGB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+      try {
+        m.enqueue(B, tokens.as<int>(), nullptr, false, 1 + engine->config.idle_steps, state.as<float>(),
+                  logits.as<float>(), hidden.as<float>(), act.as<float>(), sc, stream);
+      } catch (...) {
+        cudaStreamEndCapture(stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      NGB_CUDA(cudaStreamEndCapture(stream, &g));
+      const cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
+      cudaGraphDestroy(g);
+      cuda_check(e, "cudaGraphInstantiate");
+    }
+    NGB_CUDA(cudaGraphLaunch(graph, st));
   }
 };
 } // namespace
@@ -167,9 +192,7 @@ int ng_pool_step(void *p, const int *tokens, float *logits, float *hidden, float
     cudaStream_t st = pool.stream;
     const int B = pool.B, w = pool.engine->config.width;
     NGB_CUDA(cudaMemcpyAsync(pool.tokens.as<int>(), tokens, B * sizeof(int), cudaMemcpyHostToDevice, st));
-    m.enqueue(B, pool.tokens.as<int>(), nullptr, false, 1 + pool.engine->config.idle_steps,
-              pool.state.as<float>(), pool.logits.as<float>(), hidden ? pool.hidden.as<float>() : nullptr,
-              activity ? pool.act.as<float>() : nullptr, pool.sc, st);
+    pool.token_step(st);
     if (logits)
       NGB_CUDA(cudaMemcpyAsync(logits, pool.logits.as<float>(), size_t(B) * kVocab * 4, cudaMemcpyDeviceToHost, st));
     if (hidden)
@@ -188,8 +211,11 @@ int ng_pool_step_device(void *p, const int *d_tokens, float *d_logits, void *str
     DeviceModel &m = pool.engine->device();
     NGB_CUDA(cudaSetDevice(m.device));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : pool.stream;
-    m.enqueue(pool.B, d_tokens, nullptr, false, 1 + pool.engine->config.idle_steps, pool.state.as<float>(),
-              d_logits, nullptr, nullptr, pool.sc, st);
+    NGB_CUDA(cudaMemcpyAsync(pool.tokens.as<int>(), d_tokens, pool.B * sizeof(int), cudaMemcpyDeviceToDevice, st));
+    pool.token_step(st);
+    if (d_logits)
+      NGB_CUDA(cudaMemcpyAsync(d_logits, pool.logits.as<float>(), size_t(pool.B) * kVocab * 4,
+                               cudaMemcpyDeviceToDevice, st));
   });
 }
 

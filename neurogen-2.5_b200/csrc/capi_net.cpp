@@ -46,6 +46,7 @@ void ng_net_default_config(ng_net_config *c) {
   c->drive_p = 0.02f;
   c->drive_ns = 4.f;
   c->storage = 0;
+  c->launch = 0;
 }
 
 void *ng_net_create(const ng_net_config *cfg) {
@@ -132,6 +133,15 @@ int ng_net_run(void *net, int ticks, uint32_t *spikes, int64_t *counts) {
     auto &n = *static_cast<Network *>(net);
     std::lock_guard<std::mutex> lock(n.mutex);
     n.run_host(ticks, spikes, counts);
+  });
+}
+
+int ng_net_stats(void *net, int64_t *totals) {
+  return guarded([&] {
+    if (!net || !totals) throw std::invalid_argument("Null network or output");
+    auto &n = *static_cast<Network *>(net);
+    std::lock_guard<std::mutex> lock(n.mutex);
+    n.stats(totals);
   });
 }
 

@@ -102,6 +102,7 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
     : dims(cfg, col) {
   device = require_sm100_device();
   label = device_label(device);
+  configure_lang_kernels();
   const LangDims &d = dims;
   const size_t c = d.c, w = d.w;
 

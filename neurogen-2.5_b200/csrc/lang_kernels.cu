@@ -202,13 +202,12 @@ template <int BN, int TN> size_t gemm_smem() {
   return sizeof(float) * GM_STAGES * (GM_KC * GM_BM + BN * (GM_KC + 4));
 }
 
+template <int BN, int TN> void configure_gemm() {
+  cudaFuncSetAttribute(k_gemm<BN, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BN, TN>());
+}
+
 template <int BN, int TN> void run_gemm(const ProjArgs &a, cudaStream_t s) {
-  static bool configured = false; // per process; attribute is per function
   const size_t smem = gemm_smem<BN, TN>();
-  if (!configured) {
-    cudaFuncSetAttribute(k_gemm<BN, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured = true;
-  }
   dim3 grid((a.M + GM_BM - 1) / GM_BM, (a.B + BN - 1) / BN);
   k_gemm<BN, TN><<<grid, (GM_BM / 4) * (BN / TN), smem, s>>>(a);
 }
@@ -353,6 +352,12 @@ __global__ void k_activity(const int *counts, int A, int R, int n, int T, float 
 }
 
 } // namespace
+
+void configure_lang_kernels() {
+  configure_gemm<16, 1>();
+  configure_gemm<32, 2>();
+  configure_gemm<64, 4>();
+}
 
 void launch_projection(const ProjArgs &a, cudaStream_t s) {
   if (a.B <= 0 || a.M <= 0) return;

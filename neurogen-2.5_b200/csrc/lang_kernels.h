@@ -34,6 +34,9 @@ struct ProjArgs {
   int M, K, B;
 };
 void launch_projection(const ProjArgs &a, cudaStream_t s);
+// Per-device kernel attributes (dynamic shared memory); call once per device
+// before launching, outside any stream capture.
+void configure_lang_kernels();
 
 // One synchronous recurrent ALIF tick of one region for B sessions
 // (reference CPUBackend.cpp:20-42 with the input current assembled as in

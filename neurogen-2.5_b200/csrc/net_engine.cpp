@@ -115,6 +115,7 @@ void validate_config(const ng_net_config &c) {
     throw std::invalid_argument("Unknown drive kind");
   if (c.drive_p < 0 || c.drive_p > 1) throw std::invalid_argument("drive_p must be in [0, 1]");
   if (c.storage != 0 && c.storage != 1) throw std::invalid_argument("storage must be 0 (CSR) or 1 (BSR)");
+  if (c.launch < 0 || c.launch > 2) throw std::invalid_argument("launch must be 0 (auto), 1 (fused) or 2 (split)");
   switch (c.topology) {
   case NG_TOPO_ERDOS_RENYI:
     if (!(c.p_connect >= 0 && c.p_connect <= 1)) throw std::invalid_argument("p_connect must be in [0, 1]");
@@ -430,6 +431,13 @@ template <class T> DeviceBuffer upload_vec(const std::vector<T> &v) {
   if (!v.empty()) NGB_CUDA(cudaMemcpy(d.as<void>(), v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
   return d;
 }
+// Upload with `pad` zero elements after the data (vector loads may read past a row end).
+template <class T> DeviceBuffer upload_padded(const std::vector<T> &v, size_t pad) {
+  DeviceBuffer d((v.size() + pad) * sizeof(T));
+  NGB_CUDA(cudaMemset(d.as<void>(), 0, (v.size() + pad) * sizeof(T)));
+  if (!v.empty()) NGB_CUDA(cudaMemcpy(d.as<void>(), v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return d;
+}
 float decay_of(float dt, float tau) { return float(std::exp(-double(dt) / double(tau))); }
 } // namespace
 
@@ -454,13 +462,13 @@ Network::Network(const Topology &topo) : cfg(topo.cfg) {
     for (int x : bsr->outdeg) nnz_ += x;
   } else {
     row_ = upload_vec(csr->row);
-    syn_ = upload_vec(csr->syn);
+    syn_ = upload_padded(csr->syn, kTailPad);
     outdeg_ = upload_vec(csr->outdeg);
     if (!csr->w16.empty() || csr->w32.empty()) {
-      w_ = upload_vec(csr->w16.empty() ? std::vector<uint16_t>(csr->syn.size(), 0) : csr->w16);
+      w_ = upload_padded(csr->w16.empty() ? std::vector<uint16_t>(csr->syn.size(), 0) : csr->w16, kTailPad);
       d.w_half = 1;
     } else {
-      w_ = upload_vec(csr->w32);
+      w_ = upload_padded(csr->w32, kTailPad);
       d.w_half = 0;
     }
     d.row = row_.as<long long>();
@@ -508,11 +516,63 @@ Network::Network(const Topology &topo) : cfg(topo.cfg) {
   d.drive_thr = thr >= 4294967295.0 ? 0xFFFFFFFFu : uint32_t(thr);
   d.drive_key = mix64(c.seed ^ 0xD41Eull);
   d.ref_ticks = int(std::lround(double(c.t_ref_ms) / double(c.dt_ms)));
+  // Work list, its two counters, the current bitmask and the running totals.
+  const size_t words = (N + 31) / 32;
+  active_.reset(std::max<size_t>(N, 1) * sizeof(int2));
+  nact_.reset(2 * sizeof(unsigned));
+  bitmask_.reset(words * 4);
+  totals_.reset(2 * sizeof(unsigned long long));
+  tick_dev_.reset(sizeof(long long));
+  NGB_CUDA(cudaMemset(nact_.as<void>(), 0, 2 * sizeof(unsigned)));
+  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, words * 4));
+  NGB_CUDA(cudaMemset(totals_.as<void>(), 0, 2 * sizeof(unsigned long long)));
+  NGB_CUDA(cudaMemset(tick_dev_.as<void>(), 0, sizeof(long long)));
+  d.active = active_.as<int2>();
+  d.nact = nact_.as<unsigned>();
+  d.bitmask = bitmask_.as<uint32_t>();
+  d.totals = totals_.as<unsigned long long>();
+  // Small networks: one fused launch per tick; large: split membrane / push.
+  split_ = c.launch == 2 || (c.launch == 0 && n_ >= 65536);
+  push_blocks_ = net_push_blocks(d);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
 }
 
 Network::~Network() {
+  if (graph_) cudaGraphExecDestroy(graph_);
   if (stream) cudaStreamDestroy(stream);
+}
+
+void Network::launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st) {
+  if (split_) {
+    launch_net_alif(dev_, t, spikes_row, counts_row, st);
+    launch_net_push(dev_, t, counts_row, push_blocks_, st);
+  } else {
+    launch_net_fused(dev_, t, spikes_row, counts_row, st);
+  }
+}
+
+// One CUDA graph of kGraphTicks ticks reading the tick number from a device
+// counter (advanced by the graph's last node), so it can be replayed for any
+// starting tick.
+void Network::capture_graph() {
+  cudaGraph_t g = nullptr;
+  NGB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  for (int k = 0; k < kGraphTicks; ++k) launch_tick(TickRef{tick_dev_.as<long long>(), k}, nullptr, nullptr, stream);
+  launch_add_tick(tick_dev_.as<long long>(), kGraphTicks, stream);
+  const cudaError_t e = cudaStreamEndCapture(stream, &g);
+  if (e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cuda_check(e, "cudaStreamEndCapture");
+  }
+  const cudaError_t ie = cudaGraphInstantiate(&graph_, g, 0);
+  cudaGraphDestroy(g);
+  cuda_check(ie, "cudaGraphInstantiate");
+}
+
+void Network::stats(int64_t *totals) {
+  NGB_CUDA(cudaSetDevice(device));
+  NGB_CUDA(cudaDeviceSynchronize());
+  NGB_CUDA(cudaMemcpy(totals, totals_.as<void>(), 16, cudaMemcpyDeviceToHost));
 }
 
 void Network::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight) {
@@ -562,6 +622,7 @@ void Network::set_state(const float *v, const float *a, const float *ge, const f
   if (ref) NGB_CUDA(cudaMemcpy(ref_.as<void>(), ref, N * 4, cudaMemcpyHostToDevice));
   if (ring) NGB_CUDA(cudaMemcpy(ring_.as<void>(), ring, size_t(kRingSlots) * N * 8, cudaMemcpyHostToDevice));
   if (tick < 0) throw std::invalid_argument("tick must be non-negative");
+  NGB_CUDA(cudaMemset(nact_.as<void>(), 0, 2 * sizeof(unsigned)));
   tick_ = tick;
 }
 
@@ -582,9 +643,15 @@ void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_count
   if (ticks < 0) throw std::invalid_argument("ticks must be non-negative");
   const size_t words = (size_t(n_) + 31) / 32;
   if (d_counts) NGB_CUDA(cudaMemsetAsync(d_counts, 0, size_t(ticks) * 16, st));
-  for (int k = 0; k < ticks; ++k)
-    launch_net_tick(dev_, tick_ + k, d_spikes ? d_spikes + size_t(k) * words : nullptr,
-                    d_counts ? d_counts + 2 * size_t(k) : nullptr, st);
+  int k = 0;
+  if (!d_spikes && !d_counts && ticks >= kGraphTicks) {
+    if (!graph_) capture_graph();
+    launch_set_tick(tick_dev_.as<long long>(), tick_, st);
+    for (; k + kGraphTicks <= ticks; k += kGraphTicks) NGB_CUDA(cudaGraphLaunch(graph_, st));
+  }
+  for (; k < ticks; ++k)
+    launch_tick(TickRef{nullptr, tick_ + k}, d_spikes ? d_spikes + size_t(k) * words : nullptr,
+                d_counts ? d_counts + 2 * size_t(k) : nullptr, st);
   NGB_CUDA(cudaGetLastError());
   tick_ += ticks;
 }

@@ -67,6 +67,8 @@ public:
   // [ticks][2] (u64) are optional device outputs.
   void enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_counts, cudaStream_t st);
   void run_host(int ticks, uint32_t *spikes, int64_t *counts);
+  void stats(int64_t *totals);
+  bool split() const { return split_; }
 
   ng_net_config cfg;
   int device = 0;
@@ -81,6 +83,13 @@ private:
   DeviceBuffer row_, syn_, w_, outdeg_, bcol_, blk_, tiles_;
   DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
   DeviceBuffer rec_spikes_, rec_counts_;
+  DeviceBuffer active_, nact_, bitmask_, totals_, tick_dev_;
+  bool split_ = false;
+  int push_blocks_ = 0;
+  cudaGraphExec_t graph_ = nullptr;
+  static constexpr int kGraphTicks = 64;
+  void launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st);
+  void capture_graph();
 };
 
 } // namespace ngb

@@ -1,12 +1,22 @@
-// Isolated-tick spiking network kernels for sm_100a: one fused launch per tick.
+// Isolated-tick spiking network kernels for sm_100a.
 //
-// Each thread owns one neuron.  It reads and clears its delay-ring slot t%16,
-// advances the conductance ALIF state (neurogen/biology.py:132-180 with frozen
-// synapses), and the warp ballots its 32 spike bits into one bitmask word.
-// The same warp then pushes the outgoing synapses of each of its spiking
-// neurons (found by ffs over the ballot mask) into ring slots (t + d) % 16 with
-// integer atomics.  Delays are 1..15, so no push of tick t touches slot t%16
-// and the kernel boundary orders tick t's deliveries before tick t+1's reads.
+// One tick: every neuron reads and clears its delay-ring slot t%16, advances
+// its conductance ALIF state (neurogen/biology.py:132-180, frozen synapses),
+// and the warp ballots its 32 spike bits into one bitmask word; then the
+// outgoing synapses of every spiking neuron are pushed into ring slots
+// (t + d) % 16 with integer atomics.  Delays are 1..15, so no push of tick t
+// touches slot t%16, and the launch boundary orders tick t's deliveries before
+// tick t+1 reads its slot.
+//
+// Two launch shapes, identical arithmetic:
+//   fused  -- one kernel per tick; the warp that owns a spiking neuron pushes
+//             its synapses.  Cheapest for small networks (one launch).
+//   split  -- k_net_alif appends spiking neurons (CSR) or active 16-neuron
+//             block-columns (block storage) to a work list with one atomic per
+//             CTA, then a persistent k_net_push_* grid gives every warp one
+//             list item at a time with all of a lane's synapse loads in flight
+//             before its deliveries.  For large networks, where the push is a
+//             bandwidth problem.
 //
 // Numerics contract (shared with the C oracle, oracle/net_oracle.c): fp32
 // state, every operation rounded as written (__f*_rn intrinsics, -fmad=false),
@@ -22,6 +32,9 @@ namespace ngb {
 namespace {
 
 constexpr int TB = 256; // threads per block (8 warps)
+constexpr int WARPS = TB / 32;
+
+__device__ __forceinline__ long long tick_of(const TickRef &r) { return r.t_dev ? *r.t_dev + r.k : r.k; }
 
 __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
   z += 0x9E3779B97F4A7C15ull;
@@ -54,7 +67,41 @@ __device__ __forceinline__ float ng_expf(float x) {
   return __fmul_rn(__fmul_rn(p, __int_as_float((127 + k + 64) << 23)), 5.42101086e-20f);
 }
 
-// Fixed-point amount (2^-24 nS units) and ring component of a signed weight.
+// Membrane, conductance, adaptation and refractory update of neuron i at tick
+// t (operation order of the oracle's on_run).  Returns the spike.
+__device__ __forceinline__ bool alif_update(const NetDev &d, long long t, int i) {
+  const int slot = (int)(t & (kRingSlots - 1));
+  int2 *rp = d.ring + (size_t)slot * d.n + i;
+  const int2 r = *rp;
+  *rp = make_int2(0, 0);
+  const bool exc = i < d.n_exc;
+  float ge = __fadd_rn(__fmul_rn(d.ge[i], d.dE), __fmul_rn(__int2float_rn(r.x), kRingQuantum));
+  const float gi = __fadd_rn(__fmul_rn(d.gi[i], d.dI), __fmul_rn(__int2float_rn(r.y), kRingQuantum));
+  const bool ev = drive_event(d, t, i);
+  if (d.drive_kind == 0 && ev) ge = __fadd_rn(ge, d.drive_ns);
+  float a = __fmul_rn(d.a[i], d.dA);
+  const float g = __fadd_rn(__fadd_rn(d.g_leak, ge), gi);
+  const float vinf = __fdiv_rn(__fadd_rn(__fsub_rn(__fadd_rn(d.gLEL, __fmul_rn(d.e_inh, gi)), a), d.bias), g);
+  const int ref = d.ref[i];
+  const bool avail = ref <= 0;
+  const float cap = exc ? d.cap_e : d.cap_i;
+  const float decay = ng_expf(__fdiv_rn(__fmul_rn(d.neg_dt, g), cap));
+  float v = __fadd_rn(vinf, __fmul_rn(__fsub_rn(d.v[i], vinf), decay));
+  if (!avail) v = d.v_reset;
+  const bool s = d.drive_kind == 1 ? ev : (avail && v >= d.v_th);
+  if (s) v = d.v_reset;
+  int ref_next = ref > 0 ? ref - 1 : 0;
+  if (s) ref_next = d.ref_ticks;
+  if (s && exc) a = __fadd_rn(a, d.adapt_inc);
+  d.v[i] = v;
+  d.a[i] = a;
+  d.ge[i] = ge;
+  d.gi[i] = gi;
+  d.ref[i] = ref_next;
+  return s;
+}
+
+// Fixed-point amount (2^-24 nS units) of a signed weight.
 __device__ __forceinline__ int quantum(float w) { return __float2int_rn(__fmul_rn(fabsf(w), 16777216.f)); }
 
 __device__ __forceinline__ void deliver(const NetDev &d, long long t, uint32_t word, float w) {
@@ -70,38 +117,48 @@ __device__ __forceinline__ float half_bits(uint32_t bits16) {
 }
 
 // Push all outgoing CSR synapses of `pre` with the whole warp: each lane takes
-// 8 consecutive synapses per step (two 16-byte index loads and one 16-byte
-// fp16 weight load, or two for fp32), streaming past L1/L2 (evict-first).
-__device__ __forceinline__ void push_csr(const NetDev &d, long long t, int pre, int lane) {
+// 16 consecutive synapses per pass (four 16-byte index loads and two 16-byte
+// fp16 weight loads, or four for fp32), issued together and streamed past the
+// caches (evict-first) before any delivery.  Rows are padded to multiples of
+// 8 and the arrays carry 16 spare entries, so the loads stay in bounds; the
+// deliveries are masked to the row.
+__device__ __forceinline__ void push_row(const NetDev &d, long long t, int pre, int lane) {
   const long long e0 = d.row[pre], e1 = d.row[pre + 1];
-  for (long long e = e0 + lane * 8; e < e1; e += 256) {
+  for (long long e = e0 + lane * 16; e < e1; e += 512) {
     const uint4 *ps = reinterpret_cast<const uint4 *>(d.syn + e);
-    const uint4 p0 = __ldcs(ps), p1 = __ldcs(ps + 1);
-    const uint32_t word[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-    float w[8];
-    if (d.w_half) {
-      const uint4 wv = __ldcs(reinterpret_cast<const uint4 *>(static_cast<const __half *>(d.w) + e));
-      const uint32_t h[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint4 p[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+    for (int q = 0; q < 4; ++q) p[q] = __ldcs(ps + q);
+    float w[16];
+    if (d.w_half) {
+      const uint4 *pw = reinterpret_cast<const uint4 *>(static_cast<const __half *>(d.w) + e);
+      const uint4 w0 = __ldcs(pw), w1 = __ldcs(pw + 1);
+      const uint32_t h[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
         w[2 * j] = half_bits(h[j] & 0xFFFFu);
         w[2 * j + 1] = half_bits(h[j] >> 16);
       }
     } else {
       const float4 *pw = reinterpret_cast<const float4 *>(static_cast<const float *>(d.w) + e);
-      const float4 w0 = __ldcs(pw), w1 = __ldcs(pw + 1);
-      w[0] = w0.x; w[1] = w0.y; w[2] = w0.z; w[3] = w0.w;
-      w[4] = w1.x; w[5] = w1.y; w[6] = w1.z; w[7] = w1.w;
-    }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) deliver(d, t, word[j], w[j]);
+      for (int q = 0; q < 4; ++q) {
+        const float4 f = __ldcs(pw + q);
+        w[4 * q] = f.x; w[4 * q + 1] = f.y; w[4 * q + 2] = f.z; w[4 * q + 3] = f.w;
+      }
+    }
+    const uint32_t word[16] = {p[0].x, p[0].y, p[0].z, p[0].w, p[1].x, p[1].y, p[1].z, p[1].w,
+                               p[2].x, p[2].y, p[2].z, p[2].w, p[3].x, p[3].y, p[3].z, p[3].w};
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (e + j < e1) deliver(d, t, word[j], w[j]);
   }
 }
 
 // Push the spiking columns `sub` (16-bit mask) of block-column bc: each lane
-// takes one block, sums the selected tile columns per post row in fixed point
-// (E and I apart), and issues one atomic per non-zero row sum.
-__device__ __forceinline__ void push_bsr(const NetDev &d, long long t, int bc, unsigned sub, int lane) {
+// takes one block at a time, sums the selected tile columns per post row in
+// fixed point (E and I apart), and issues one atomic per non-zero row sum.
+__device__ __forceinline__ void push_block_column(const NetDev &d, long long t, int bc, unsigned sub, int lane) {
   const long long b0 = d.bcol[bc], b1 = d.bcol[bc + 1];
   for (long long b = b0 + lane; b < b1; b += 32) {
     const uint32_t meta = __ldcs(d.blk + b);
@@ -138,92 +195,160 @@ __device__ __forceinline__ void push_bsr(const NetDev &d, long long t, int bc, u
   }
 }
 
-template <bool BSR>
-__global__ void __launch_bounds__(TB) k_net_tick(NetDev d, long long t, uint32_t *spikes_out,
-                                                 unsigned long long *counts) {
-  __shared__ unsigned long long red[2][TB / 32];
-  const int i = blockIdx.x * TB + threadIdx.x;
+// CTA-wide sum of one value per warp (lane 0 contributes), added once to the
+// running total and, when given, to this tick's counter.
+__device__ __forceinline__ void add_block_count(unsigned long long v, unsigned long long *total,
+                                                unsigned long long *tick_count) {
+  __shared__ unsigned long long part[WARPS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  bool s = false;
-  int events = 0;
-  if (i < d.n) {
-    const int slot = (int)(t & (kRingSlots - 1));
-    int2 *rp = d.ring + (size_t)slot * d.n + i;
-    const int2 r = *rp;
-    *rp = make_int2(0, 0);
-    const bool exc = i < d.n_exc;
-    float ge = __fadd_rn(__fmul_rn(d.ge[i], d.dE), __fmul_rn(__int2float_rn(r.x), kRingQuantum));
-    const float gi = __fadd_rn(__fmul_rn(d.gi[i], d.dI), __fmul_rn(__int2float_rn(r.y), kRingQuantum));
-    const bool ev = drive_event(d, t, i);
-    if (d.drive_kind == 0 && ev) ge = __fadd_rn(ge, d.drive_ns);
-    float a = __fmul_rn(d.a[i], d.dA);
-    const float g = __fadd_rn(__fadd_rn(d.g_leak, ge), gi);
-    const float vinf = __fdiv_rn(__fadd_rn(__fsub_rn(__fadd_rn(d.gLEL, __fmul_rn(d.e_inh, gi)), a), d.bias), g);
-    const int ref = d.ref[i];
-    const bool avail = ref <= 0;
-    const float cap = exc ? d.cap_e : d.cap_i;
-    const float decay = ng_expf(__fdiv_rn(__fmul_rn(d.neg_dt, g), cap));
-    float v = __fadd_rn(vinf, __fmul_rn(__fsub_rn(d.v[i], vinf), decay));
-    if (!avail) v = d.v_reset;
-    s = d.drive_kind == 1 ? ev : (avail && v >= d.v_th);
-    if (s) v = d.v_reset;
-    int ref_next = ref > 0 ? ref - 1 : 0;
-    if (s) ref_next = d.ref_ticks;
-    if (s && exc) a = __fadd_rn(a, d.adapt_inc);
-    d.v[i] = v;
-    d.a[i] = a;
-    d.ge[i] = ge;
-    d.gi[i] = gi;
-    d.ref[i] = ref_next;
-    if (s && counts) events = d.outdeg[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  if (lane == 0) part[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long s = 0;
+    for (int k = 0; k < WARPS; ++k) s += part[k];
+    if (s) {
+      atomicAdd(total, s);
+      if (tick_count) atomicAdd(tick_count, s);
+    }
   }
+  __syncthreads();
+}
+
+template <bool BSR>
+__global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t *spikes_out,
+                                                  unsigned long long *counts) {
+  const long long t = tick_of(tr);
+  const int i = blockIdx.x * TB + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool s = i < d.n ? alif_update(d, t, i) : false;
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
-  if (spikes_out && lane == 0 && base < d.n) spikes_out[base >> 5] = fired;
+  if (lane == 0 && base < d.n) {
+    d.bitmask[base >> 5] = fired;
+    if (spikes_out) spikes_out[base >> 5] = fired;
+  }
+  unsigned long long events = 0;
   if (BSR) {
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const unsigned sub = (fired >> (16 * half)) & 0xFFFFu;
-      if (sub) push_bsr(d, t, (base >> 4) + half, sub, lane);
+      if (sub) push_block_column(d, t, (base >> 4) + half, sub, lane);
     }
   } else {
     unsigned m = fired;
     while (m) {
       const int src = __ffs(m) - 1;
       m &= m - 1;
-      push_csr(d, t, base + src, lane);
+      push_row(d, t, base + src, lane);
     }
   }
-  if (counts) {
-    unsigned long long ev = (unsigned long long)events;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ev += __shfl_down_sync(0xffffffffu, ev, o);
-    if (lane == 0) {
-      red[0][warp] = __popc(fired);
-      red[1][warp] = ev;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned long long ns = 0, ne = 0;
-      for (int k = 0; k < TB / 32; ++k) {
-        ns += red[0][k];
-        ne += red[1][k];
-      }
-      if (ns) {
-        atomicAdd(counts, ns);
-        atomicAdd(counts + 1, ne);
-      }
-    }
-  }
+  if (s) events = (unsigned long long)d.outdeg[i];
+  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals, counts);
+  add_block_count(events, d.totals + 1, counts ? counts + 1 : nullptr);
 }
+
+template <bool BSR>
+__global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t *spikes_out,
+                                                 unsigned long long *counts) {
+  __shared__ unsigned warp_items[WARPS];
+  __shared__ unsigned block_base;
+  const long long t = tick_of(tr);
+  const int par = (int)(t & 1);
+  const int i = blockIdx.x * TB + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool s = i < d.n ? alif_update(d, t, i) : false;
+  const unsigned fired = __ballot_sync(0xffffffffu, s);
+  const int base = i - lane;
+  if (lane == 0 && base < d.n) {
+    d.bitmask[base >> 5] = fired;
+    if (spikes_out) spikes_out[base >> 5] = fired;
+  }
+  // Work items of this warp: its spiking neurons, or its non-empty halves.
+  const unsigned sub0 = fired & 0xFFFFu, sub1 = fired >> 16;
+  const unsigned items = BSR ? (unsigned)(sub0 != 0) + (unsigned)(sub1 != 0) : (unsigned)__popc(fired);
+  if (lane == 0) warp_items[warp] = items;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned total = 0;
+    for (int k = 0; k < WARPS; ++k) {
+      const unsigned c = warp_items[k];
+      warp_items[k] = total;
+      total += c;
+    }
+    block_base = total ? atomicAdd(d.nact + par, total) : 0;
+  }
+  __syncthreads();
+  const unsigned at = block_base + warp_items[warp];
+  if (BSR) {
+    if (lane == 0) {
+      unsigned k = at;
+      if (sub0) d.active[k++] = make_int2(base >> 4, (int)sub0);
+      if (sub1) d.active[k] = make_int2((base >> 4) + 1, (int)sub1);
+    }
+  } else if (s) {
+    d.active[at + __popc(fired & ((1u << lane) - 1u))] = make_int2(i, 0);
+  }
+  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals, counts);
+}
+
+template <bool BSR>
+__global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned long long *counts) {
+  const long long t = tick_of(tr);
+  const int par = (int)(t & 1);
+  const int lane = threadIdx.x & 31;
+  const unsigned n_act = d.nact[par];
+  if (blockIdx.x == 0 && threadIdx.x == 0) d.nact[par ^ 1] = 0; // next tick's list starts empty
+  const unsigned stride = gridDim.x * WARPS;
+  unsigned long long events = 0;
+  for (unsigned a = blockIdx.x * WARPS + (threadIdx.x >> 5); a < n_act; a += stride) {
+    const int2 item = d.active[a];
+    if (BSR) {
+      push_block_column(d, t, item.x, (unsigned)item.y, lane);
+      if (lane < 16 && ((unsigned)item.y >> lane & 1u)) events += (unsigned long long)d.outdeg[item.x * 16 + lane];
+    } else {
+      push_row(d, t, item.x, lane);
+      if (lane == 0) events += (unsigned long long)d.outdeg[item.x];
+    }
+  }
+  add_block_count(events, d.totals + 1, counts ? counts + 1 : nullptr);
+}
+
+__global__ void k_set_tick(long long *t, long long v) { *t = v; }
+__global__ void k_add_tick(long long *t, long long dv) { *t += dv; }
 
 } // namespace
 
-void launch_net_tick(const NetDev &d, long long t, uint32_t *spikes_out, unsigned long long *counts,
+void launch_net_fused(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
+                      cudaStream_t s) {
+  const int blocks = (d.n + TB - 1) / TB;
+  if (d.bsr) k_net_fused<true><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
+  else k_net_fused<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
+}
+
+void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
                      cudaStream_t s) {
   const int blocks = (d.n + TB - 1) / TB;
-  if (d.bsr) k_net_tick<true><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
-  else k_net_tick<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
+  if (d.bsr) k_net_alif<true><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
+  else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
 }
+
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int push_blocks, cudaStream_t s) {
+  if (d.bsr) k_net_push<true><<<push_blocks, TB, 0, s>>>(d, t, counts);
+  else k_net_push<false><<<push_blocks, TB, 0, s>>>(d, t, counts);
+}
+
+int net_push_blocks(const NetDev &d) {
+  int dev = 0, sms = 0, per = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (d.bsr) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_net_push<true>, TB, 0);
+  else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_net_push<false>, TB, 0);
+  return sms * (per > 0 ? per : 1);
+}
+
+void launch_set_tick(long long *t_dev, long long value, cudaStream_t s) { k_set_tick<<<1, 1, 0, s>>>(t_dev, value); }
+void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s) { k_add_tick<<<1, 1, 0, s>>>(t_dev, delta); }
 
 } // namespace ngb

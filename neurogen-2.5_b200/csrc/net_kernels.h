@@ -7,6 +7,8 @@ namespace ngb {
 
 constexpr int kRingSlots = 16; // delay ring depth; delays 1..15 ticks
 constexpr float kRingQuantum = 5.9604644775390625e-08f; // 2^-24 nS per ring unit
+constexpr int kRowPad = 8;     // CSR rows padded to multiples of 8 synapses
+constexpr int kTailPad = 16;   // extra zero synapses after the last row
 
 // Synapse word: postsynaptic index in bits 0-27, (delay - 1) in bits 28-31.
 constexpr uint32_t kPostMask = 0x0FFFFFFFu;
@@ -28,6 +30,13 @@ struct NetDev {
   float *v, *a, *ge, *gi;
   int *ref;
   int2 *ring;
+  // Per-tick work list of the split path: spiking neurons (CSR) or
+  // (block-column, 16-bit spike mask) pairs (blocks), with two counters used
+  // alternately by even and odd ticks.
+  int2 *active;
+  unsigned *nact;               // [2]
+  uint32_t *bitmask;            // this tick's spike words [ceil(n/32)]
+  unsigned long long *totals;   // [2] spikes, synaptic events since creation
   // Constants (see net_kernels.cu for the exact operation order).
   float dE, dI, dA, g_leak, gLEL, e_inh, v_th, v_reset, cap_e, cap_i, neg_dt, adapt_inc, bias,
       drive_ns;
@@ -37,11 +46,23 @@ struct NetDev {
   int ref_ticks;
 };
 
-// One tick t: ALIF update of every neuron, spike bitmask by warp ballot,
-// push of every spiking neuron's synapses into ring slots (t + d) % 16.
-// spikes_out: this tick's ceil(n/32) bit words or null.  counts: [2] u64
-// accumulators (spikes, synaptic events) or null.
-void launch_net_tick(const NetDev &d, long long t, uint32_t *spikes_out,
-                     unsigned long long *counts, cudaStream_t s);
+// Which tick a launch computes: *t_dev + k when t_dev is set (graph replay
+// with a device-resident tick counter), else k.
+struct TickRef {
+  const long long *t_dev;
+  long long k;
+};
+
+// Fused single launch per tick (small networks): ALIF, ballot, push.
+void launch_net_fused(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
+                      cudaStream_t s);
+// Split path (large networks): ALIF + bitmask + work list, then the push.
+void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
+                     cudaStream_t s);
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int push_blocks,
+                     cudaStream_t s);
+int net_push_blocks(const NetDev &d); // persistent grid size of the push kernel
+void launch_set_tick(long long *t_dev, long long value, cudaStream_t s);
+void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s);
 
 } // namespace ngb

@@ -30,6 +30,8 @@ def default_config(**overrides):
             value = DRIVE[value]
         elif key == 'storage' and isinstance(value, str):
             value = {'csr': 0, 'bsr': 1}[value]
+        elif key == 'launch' and isinstance(value, str):
+            value = {'auto': 0, 'fused': 1, 'split': 2}[value]
         if not hasattr(cfg, key):
             raise KeyError(key)
         setattr(cfg, key, value)
@@ -115,6 +117,16 @@ class Network:
         self._check(self.lib.ng_net_get_state(self.h, ptr(v), ptr(a), ptr(ge), ptr(gi), ptr(ref),
                                               ptr(ring), ptr(tick)))
         return dict(v=v, a=a, ge=ge, gi=gi, ref=ref, ring=ring, tick=int(tick[0]))
+
+    def stats(self):
+        """(spikes, synaptic events) delivered since creation."""
+        out = np.zeros(2, np.int64)
+        self._check(self.lib.ng_net_stats(self.h, out))
+        return int(out[0]), int(out[1])
+
+    def run_device(self, ticks, stream=0):
+        """Enqueue ticks on a CUDA stream handle (graph replay; no host copies)."""
+        self._check(self.lib.ng_net_run_device(self.h, ticks, None, None, stream or None))
 
     def run(self, ticks, record=True):
         """-> (spike words uint32 [ticks, words] or None, counts int64 [ticks, 2])."""

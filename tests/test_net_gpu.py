@@ -36,8 +36,10 @@ def assert_same_state(net, orc):
     assert a['tick'] == b['tick']
 
 
-def test_isolated_8k_bit_exact_200_ticks():
+@pytest.mark.parametrize('launch', ['fused', 'split'])
+def test_isolated_8k_bit_exact_200_ticks(launch):
     cfg = isolated_8k()
+    cfg.launch = {'fused': 1, 'split': 2}[launch]
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 200)
     assert oc[:, 0].sum() > 1000
     np.testing.assert_array_equal(gs, os_)  # every spike of every tick
@@ -45,33 +47,36 @@ def test_isolated_8k_bit_exact_200_ticks():
     assert_same_state(net, orc)
 
 
+@pytest.mark.parametrize('launch', ['fused', 'split'])
 @pytest.mark.parametrize('storage', ['csr', 'bsr'])
-def test_block_matrix_both_storages_bit_exact(storage):
+def test_block_matrix_both_storages_bit_exact(storage, launch):
     cfg = default_config(n=4096, n_exc=3277, topology='bsr16', bsr_blocks=32, bsr_fill=64,
                          weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, storage=storage,
-                         drive_kind='imposed', drive_p=0.03, seed=4)
+                         drive_kind='imposed', drive_p=0.03, seed=4, launch=launch)
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 60)
     np.testing.assert_array_equal(gs, os_)
     np.testing.assert_array_equal(gc, oc)
     assert_same_state(net, orc)
 
 
-def test_fixed_fanin_fp16_imposed_bit_exact():
+@pytest.mark.parametrize('launch', ['fused', 'split'])
+def test_fixed_fanin_fp16_imposed_bit_exact(launch):
     cfg = default_config(n=16384, n_exc=13107, topology='fixed_fanin', fanin=128, weight_kind='halfnormal_f16',
-                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8)
+                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8, launch=launch)
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 40)
     np.testing.assert_array_equal(gs, os_)
     np.testing.assert_array_equal(gc, oc)
     assert_same_state(net, orc)
 
 
-def test_ragged_sizes_and_empty_network():
+@pytest.mark.parametrize('launch', ['fused', 'split'])
+def test_ragged_sizes_and_empty_network(launch):
     # n not a multiple of 32 (partial last warp) and an empty synapse set.
-    cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3)
+    cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3, launch=launch)
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 50)
     np.testing.assert_array_equal(gs, os_)
     assert_same_state(net, orc)
-    cfg0 = default_config(n=37, n_exc=30, p_connect=0.0, drive_ns=30.0, drive_p=0.2, seed=1)
+    cfg0 = default_config(n=37, n_exc=30, p_connect=0.0, drive_ns=30.0, drive_p=0.2, seed=1, launch=launch)
     net, orc, (gs, gc), (os_, oc) = run_both(cfg0, 20)
     assert Topology(cfg0).synapses == 0
     np.testing.assert_array_equal(gs, os_)
@@ -141,3 +146,25 @@ def test_scaled_262k_csr_properties():
         sel = fired[k][pre] & (k + delay >= 6)
         pending += q[sel].sum()
     assert net.get_state()['ring'].astype(np.int64).sum() == pending
+
+
+@pytest.mark.parametrize('launch', ['fused', 'split'])
+def test_graph_replay_equals_recorded_run(launch):
+    """The graph path (no per-tick outputs, device tick counter) and the recorded path give the
+    same state, totals and trajectory, including a run length that is not a multiple of the
+    graph length and a resume from an arbitrary tick."""
+    cfg = isolated_8k(seed=5)
+    cfg.launch = {'fused': 1, 'split': 2}[launch]
+    topo = Topology(cfg)
+    a, b = topo.network(), topo.network()
+    _, ca = a.run(150)
+    b.run_device(150)
+    sa, sb = a.get_state(), b.get_state()
+    for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
+        assert np.array_equal(sa[k], sb[k]), k
+    assert sa['tick'] == sb['tick'] == 150
+    assert b.stats() == (int(ca[:, 0].sum()), int(ca[:, 1].sum()))
+    b.run_device(70)
+    _, _ = a.run(70)
+    sa, sb = a.get_state(), b.get_state()
+    assert all(np.array_equal(sa[k], sb[k]) for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'))
