@@ -51,6 +51,7 @@ def parse():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--ticks', type=int, default=0, help='override ticks per step (profiling runs)')
+    p.add_argument('--tokens', type=int, default=0, help='override tokens per step (profiling runs)')
     return p.parse_args()
 
 
@@ -194,7 +195,7 @@ def bench_ticks(args, dist):
     net = topo.network()
     setup_s = time.time() - t0
     split = cfg.launch == 2 or (cfg.launch == 0 and cfg.n >= 65536)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
         if lib.ng_net_run_device(net.h, ticks, None, None, stream.cuda_stream):
@@ -246,28 +247,27 @@ def bench_ticks(args, dist):
 
 def e2e_ticks(args, lib, net, cfg, ticks, dist):
     """Through the C ABI with host buffers: per step, upload the full network state from
-    pinned host memory, run the ticks, read back the per-tick counts and the state."""
+    pinned host memory, run the ticks, read back the spike/event totals and the state."""
     import ctypes as ct
     import torch
-    n = cfg.n
     pin = lambda shape, dt: torch.empty(shape, dtype=dt, pin_memory=True).numpy()
     st = net.get_state()
-    host = {k: pin(st[k].shape, torch.float32 if st[k].dtype == np.float32 else torch.int32)
-            for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')}
-    for k in host:
+    names = ('v', 'a', 'ge', 'gi', 'ref', 'ring')
+    host = {k: pin(st[k].shape, torch.float32 if st[k].dtype == np.float32 else torch.int32) for k in names}
+    for k in names:
         host[k][...] = st[k]
-    counts = pin((ticks, 2), torch.int64)
+    totals = pin((2,), torch.int64)
     ptr = lambda a: a.ctypes.data_as(ct.c_void_p)
-    h2d = sum(host[k].nbytes for k in host)
-    d2h = h2d + counts.nbytes
+    h2d = sum(host[k].nbytes for k in names)
+    d2h = h2d + totals.nbytes
 
     def step():
         t0 = time.perf_counter()
-        if lib.ng_net_set_state(net.h, *[ptr(host[k]) for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')], st['tick']):
+        if lib.ng_net_set_state(net.h, *[ptr(host[k]) for k in names], st['tick']):
             raise RuntimeError(lib.ng_error().decode())
-        if lib.ng_net_run(net.h, ticks, None, ptr(counts)):
+        if lib.ng_net_run(net.h, ticks, None, None):
             raise RuntimeError(lib.ng_error().decode())
-        if lib.ng_net_get_state(net.h, *[ptr(host[k]) for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')], None):
+        if lib.ng_net_stats(net.h, totals) or lib.ng_net_get_state(net.h, *[ptr(host[k]) for k in names], None):
             raise RuntimeError(lib.ng_error().decode())
         return time.perf_counter() - t0
 
@@ -278,7 +278,7 @@ def e2e_ticks(args, lib, net, cfg, ticks, dist):
     t_max = dist.max(elapsed)
     return {'value': ticks * args.steps * dist.world / t_max, 'unit': 'ticks/s',
             'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
-            'api': 'ng_net_set_state + ng_net_run + ng_net_get_state (host buffers)'}
+            'api': 'ng_net_set_state + ng_net_run + ng_net_stats + ng_net_get_state (host buffers)'}
 
 
 def cpu_baseline_ticks(cfg, topo, budget_s=12.0):
@@ -353,12 +353,12 @@ def bench_lang(args, dist):
         per = SESSIONS // dist.world
         mine = list(range(dist.rank * per, (dist.rank + 1) * per))
     B = len(mine)
-    T = LANG_TOKENS_PER_STEP[args.workload]
+    T = args.tokens or LANG_TOKENS_PER_STEP[args.workload]
     toks = lang_tokens(args.workload, mine, 1024 if args.workload == 'sessions' else 512)
     pool = lib.ng_pool_create(eng.handle, B)
     if not pool:
         raise RuntimeError(lib.ng_error().decode())
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
     d_tok = torch.from_numpy(np.ascontiguousarray(toks)).cuda()
     d_logits = torch.empty((B, 264), device='cuda')
     pos = [0]
