@@ -193,17 +193,22 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
     // Feedback projections of every region read only that region's memory,
     // which the region updates after it has used them, so all regions'
     // feedback for this advance can be computed up front.
-    for (int r = 0; r < d.R; ++r) {
-      ProjArgs fa{};
-      fa.wp = regions[r].fb_wp.as<float>();
-      fa.x = d_state + r * d.RS + 4L * d.n;
-      fa.ldx = d.S;
-      fa.y = sc.fb.as<float>() + size_t(r) * B * Mfb;
-      fa.ldy = Mfb;
-      fa.M = Mfb;
-      fa.K = d.w;
-      fa.B = B;
-      launch_projection(fa, st);
+    for (int r0 = 0; r0 < d.R; r0 += 4) {
+      ProjBatch fb{};
+      fb.count = std::min(4, d.R - r0);
+      for (int z = 0; z < fb.count; ++z) {
+        const int r = r0 + z;
+        ProjArgs &fa = fb.a[z];
+        fa.wp = regions[r].fb_wp.as<float>();
+        fa.x = d_state + r * d.RS + 4L * d.n;
+        fa.ldx = d.S;
+        fa.y = sc.fb.as<float>() + size_t(r) * B * Mfb;
+        fa.ldy = Mfb;
+        fa.M = Mfb;
+        fa.K = d.w;
+        fa.B = B;
+      }
+      launch_projections(fb, st);
     }
     for (int r = 0; r < d.R; ++r) {
       const RegionWeights &g = regions[r];

@@ -22,6 +22,7 @@
 
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 
 namespace ngb {
 namespace {
@@ -65,90 +66,106 @@ __device__ __forceinline__ float host_tanh(float x) {
 }
 
 // ---------------------------------------------------------------------------
-// Projection, batch 1: one warp per 32-row panel, one lane per row.  The
-// panel's [K][32] weights stream through an 8-stage cp.async ring so the
-// strictly sequential accumulation chain never waits on L2.
+// Projection, batch 1: one warp per 8 rows (a quarter of a 32-row panel); lanes
+// 0-7 each own one row's sequential chain.  The quarter-panel's weights (32
+// bytes per k) stream through a deep cp.async ring (GV_STAGES x GV_KC k) so
+// that most of a row block is in flight at once and the chain, not L2
+// latency, sets the time.
 // ---------------------------------------------------------------------------
-constexpr int GV_KC = 32, GV_STAGES = 8;
+constexpr int GV_ROWS = 8, GV_KC = 64, GV_STAGES = 24;
+constexpr int GV_STAGE_FLOATS = GV_KC * GV_ROWS + GV_KC;
 
-__global__ void __launch_bounds__(32) k_gemv(ProjArgs a) {
-  __shared__ __align__(16) float ws[GV_STAGES][GV_KC * 32];
-  __shared__ __align__(16) float xs[GV_STAGES][GV_KC];
-  const int p = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
-  const int m = p * 32 + lane;
-  const float *x = a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx;
-  const float *wpan = a.wp + (size_t)p * a.K * 32;
+__global__ void __launch_bounds__(32) k_gemv(ProjBatch pb) {
+  extern __shared__ __align__(16) float gv[];
+  const ProjArgs &a = pb.a[blockIdx.z];
+  const int q = blockIdx.x, p = q >> 2, r0 = (q & 3) * GV_ROWS, lane = threadIdx.x;
+  if (p * 32 >= a.M) return;
+  const int m = p * 32 + r0 + lane;
+  const float *x = a.x + (long)(a.xidx ? a.xidx[0] : 0) * a.ldx;
+  const float *wq = a.wp + (size_t)p * a.K * 32 + r0;
   const int nch = (a.K + GV_KC - 1) / GV_KC;
   auto issue = [&](int ch) {
     if (ch < nch) {
       const int k0 = ch * GV_KC, kc = min(GV_KC, a.K - k0);
-      const float *src = wpan + (size_t)k0 * 32;
-      float *dst = ws[ch % GV_STAGES];
-      for (int i = lane; i < kc * 8; i += 32) cp_async16(dst + i * 4, src + i * 4);
-      for (int i = lane; i < kc; i += 32) cp_async4(&xs[ch % GV_STAGES][i], x + k0 + i);
+      float *ws = gv + (ch % GV_STAGES) * GV_STAGE_FLOATS;
+      float *xs = ws + GV_KC * GV_ROWS;
+      for (int i = lane; i < kc * 2; i += 32) // two 16-byte pieces per k
+        cp_async16(ws + (i >> 1) * GV_ROWS + (i & 1) * 4, wq + (size_t)(k0 + (i >> 1)) * 32 + (i & 1) * 4);
+      for (int i = lane; i < kc; i += 32) cp_async4(xs + i, x + k0 + i);
     }
     cp_async_commit();
   };
-#pragma unroll
   for (int s = 0; s < GV_STAGES - 1; ++s) issue(s);
-  float acc = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+  float acc = (a.bias && lane < GV_ROWS && m < a.M) ? a.bias[m] : 0.f;
   for (int ch = 0; ch < nch; ++ch) {
     issue(ch + GV_STAGES - 1);
     cp_async_wait<GV_STAGES - 1>();
     __syncwarp();
-    const float *w = ws[ch % GV_STAGES];
-    const float *xv = xs[ch % GV_STAGES];
-    const int kc = min(GV_KC, a.K - ch * GV_KC);
-    if (kc == GV_KC) {
+    const float *ws = gv + (ch % GV_STAGES) * GV_STAGE_FLOATS;
+    const float *xs = ws + GV_KC * GV_ROWS;
+    if (lane < GV_ROWS) {
+      const int kc = min(GV_KC, a.K - ch * GV_KC);
+      if (kc == GV_KC) {
 #pragma unroll
-      for (int k = 0; k < GV_KC; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k * 32 + lane], xv[k]));
-    } else {
-      for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k * 32 + lane], xv[k]));
+        for (int k = 0; k < GV_KC; ++k) acc = __fadd_rn(acc, __fmul_rn(ws[k * GV_ROWS + lane], xs[k]));
+      } else {
+        for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(ws[k * GV_ROWS + lane], xs[k]));
+      }
     }
     __syncwarp();
   }
-  if (m < a.M) {
-    if (a.addv) acc = __fadd_rn(acc, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
-    a.y[(long)b * a.ldy + m] = acc;
+  if (lane < GV_ROWS && m < a.M) {
+    if (a.addv) acc = __fadd_rn(acc, __fmul_rn(0.25f, a.addv[m]));
+    a.y[m] = acc;
   }
 }
 
 // ---------------------------------------------------------------------------
-// Projection, batch >= 2: CTA tile BM rows x BN sessions, 4 rows x TN
-// sessions per thread, K staged in KC chunks through a cp.async ring.  Each
-// output is still one sequential chain over k (no split-K), so the result is
-// identical to the batch-1 kernel and to the CPU.
+// Projection, batch >= 2: CTA tile = one 32-row panel x BN sessions; each
+// thread owns 4 rows x TN sessions (4*TN independent chains), so the FP32
+// pipe stays busy while each chain waits on its previous add.  K is staged
+// in 32-wide chunks through a 4-stage cp.async ring; the session operand is
+// stored k-major so a thread's TN sessions are one vector load.  Every
+// output is still one sequential chain over k (no split-K): results equal
+// the batch-1 kernel's and the CPU's bit for bit.
 // ---------------------------------------------------------------------------
-constexpr int GM_KC = 32, GM_STAGES = 4, GM_BM = 64;
+constexpr int GM_KC = 32, GM_STAGES = 4;
+
+template <int BN, int TN> __host__ __device__ constexpr int gemm_threads() { return 8 * (BN / TN); }
+template <int BN> __host__ __device__ constexpr int gemm_stage_floats() { return GM_KC * 32 + GM_KC * BN; }
+
+template <int TN> struct VecT;
+template <> struct VecT<1> { using T = float; };
+template <> struct VecT<2> { using T = float2; };
+template <> struct VecT<4> { using T = float4; };
+
+template <int TN>
+__device__ __forceinline__ void load_x(const float *p, float (&x)[TN]) {
+  const typename VecT<TN>::T v = *reinterpret_cast<const typename VecT<TN>::T *>(p);
+  const float *f = reinterpret_cast<const float *>(&v);
+#pragma unroll
+  for (int s = 0; s < TN; ++s) x[s] = f[s];
+}
 
 template <int BN, int TN>
-__global__ void __launch_bounds__((GM_BM / 4) * (BN / TN)) k_gemm(ProjArgs a) {
-  constexpr int BM = GM_BM, KC = GM_KC, TX = BM / 4, TY = BN / TN, NT = TX * TY;
-  constexpr int XLD = KC + 4;
-  constexpr int WS = KC * BM, XS = BN * XLD, STAGE = WS + XS;
+__global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
+  constexpr int NT = gemm_threads<BN, TN>(), STAGE = gemm_stage_floats<BN>();
   extern __shared__ __align__(16) float sm[];
-  const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
-  const int m0 = blockIdx.x * BM, b0 = blockIdx.y * BN;
-  const int P = (a.M + 31) / 32;
-  const int nch = (a.K + KC - 1) / KC;
+  const ProjArgs &a = pb.a[blockIdx.z];
+  const int p = blockIdx.x, b0 = blockIdx.y * BN;
+  if (p * 32 >= a.M || b0 >= a.B) return;
+  const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+  const int nch = (a.K + GM_KC - 1) / GM_KC;
+  const float *wpan = a.wp + (size_t)p * a.K * 32;
   auto issue = [&](int ch) {
     if (ch < nch) {
-      const int k0 = ch * KC, kc = min(KC, a.K - k0);
+      const int k0 = ch * GM_KC, kc = min(GM_KC, a.K - k0);
       float *ws = sm + (ch % GM_STAGES) * STAGE;
-      float *xs = ws + WS;
-      const int wpieces = (BM / 32) * kc * 8;
-      for (int i = tid; i < wpieces; i += NT) {
-        const int q = i / (kc * 8), r = i % (kc * 8), k = r / 8, j4 = r % 8;
-        const int pan = m0 / 32 + q;
-        if (pan < P)
-          cp_async16(ws + k * BM + q * 32 + j4 * 4, a.wp + ((size_t)pan * a.K + k0 + k) * 32 + j4 * 4);
-      }
+      float *xs = ws + GM_KC * 32;
+      for (int i = tid; i < kc * 8; i += NT) cp_async16(ws + i * 4, wpan + (size_t)k0 * 32 + i * 4);
       for (int i = tid; i < BN * kc; i += NT) {
-        const int s = i / kc, k = i % kc, b = b0 + s;
-        if (b < a.B) {
-          const float *xr = a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx;
-          cp_async4(xs + s * XLD + k, xr + k0 + k);
-        }
+        const int sidx = i / kc, k = i - sidx * kc, b = b0 + sidx;
+        if (b < a.B) cp_async4(xs + k * BN + sidx, a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx + k0 + k);
       }
     }
     cp_async_commit();
@@ -158,7 +175,7 @@ __global__ void __launch_bounds__((GM_BM / 4) * (BN / TN)) k_gemm(ProjArgs a) {
   float acc[4][TN];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int m = m0 + tx * 4 + i;
+    const int m = p * 32 + tx * 4 + i;
     const float init = (a.bias && m < a.M) ? a.bias[m] : 0.f;
 #pragma unroll
     for (int s = 0; s < TN; ++s) acc[i][s] = init;
@@ -168,24 +185,29 @@ __global__ void __launch_bounds__((GM_BM / 4) * (BN / TN)) k_gemm(ProjArgs a) {
     cp_async_wait<GM_STAGES - 1>();
     __syncthreads();
     const float *ws = sm + (ch % GM_STAGES) * STAGE;
-    const float *xs = ws + WS;
-    const int kc = min(KC, a.K - ch * KC);
-    for (int k = 0; k < kc; ++k) {
-      const float4 wv = *reinterpret_cast<const float4 *>(ws + k * BM + tx * 4);
+    const float *xs = ws + GM_KC * 32;
+    const int kc = min(GM_KC, a.K - ch * GM_KC);
+    auto step = [&](int k) {
+      const float4 wv = *reinterpret_cast<const float4 *>(ws + k * 32 + tx * 4);
       const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
       float xr[TN];
-#pragma unroll
-      for (int s = 0; s < TN; ++s) xr[s] = xs[(ty * TN + s) * XLD + k];
+      load_x<TN>(xs + k * BN + ty * TN, xr);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int s = 0; s < TN; ++s) acc[i][s] = __fadd_rn(acc[i][s], __fmul_rn(w4[i], xr[s]));
+    };
+    if (kc == GM_KC) {
+#pragma unroll
+      for (int k = 0; k < GM_KC; ++k) step(k);
+    } else {
+      for (int k = 0; k < kc; ++k) step(k);
     }
     __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int m = m0 + tx * 4 + i;
+    const int m = p * 32 + tx * 4 + i;
 #pragma unroll
     for (int s = 0; s < TN; ++s) {
       const int b = b0 + ty * TN + s;
@@ -198,18 +220,15 @@ __global__ void __launch_bounds__((GM_BM / 4) * (BN / TN)) k_gemm(ProjArgs a) {
   }
 }
 
-template <int BN, int TN> size_t gemm_smem() {
-  return sizeof(float) * GM_STAGES * (GM_KC * GM_BM + BN * (GM_KC + 4));
-}
+template <int BN, int TN> size_t gemm_smem() { return sizeof(float) * GM_STAGES * gemm_stage_floats<BN>(); }
 
 template <int BN, int TN> void configure_gemm() {
   cudaFuncSetAttribute(k_gemm<BN, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BN, TN>());
 }
 
-template <int BN, int TN> void run_gemm(const ProjArgs &a, cudaStream_t s) {
-  const size_t smem = gemm_smem<BN, TN>();
-  dim3 grid((a.M + GM_BM - 1) / GM_BM, (a.B + BN - 1) / BN);
-  k_gemm<BN, TN><<<grid, (GM_BM / 4) * (BN / TN), smem, s>>>(a);
+template <int BN, int TN> void run_gemm(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
+  dim3 grid((max_m + 31) / 32, (max_b + BN - 1) / BN, pb.count);
+  k_gemm<BN, TN><<<grid, gemm_threads<BN, TN>(), gemm_smem<BN, TN>(), s>>>(pb);
 }
 
 // ---------------------------------------------------------------------------
@@ -354,24 +373,55 @@ __global__ void k_activity(const int *counts, int A, int R, int n, int T, float 
 } // namespace
 
 void configure_lang_kernels() {
-  configure_gemm<16, 1>();
-  configure_gemm<32, 2>();
+  configure_gemm<8, 1>();
+  configure_gemm<16, 2>();
+  configure_gemm<32, 4>();
   configure_gemm<64, 4>();
+  cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)(sizeof(float) * GV_STAGES * GV_STAGE_FLOATS));
+}
+
+void launch_projections(const ProjBatch &pb, cudaStream_t s) {
+  int max_m = 0, max_b = 0;
+  for (int z = 0; z < pb.count; ++z) {
+    max_m = max(max_m, pb.a[z].M);
+    max_b = max(max_b, pb.a[z].B);
+  }
+  if (max_m <= 0 || max_b <= 0) return;
+  if (max_b == 1) {
+    dim3 grid(((max_m + 31) / 32) * 4, 1, pb.count);
+    k_gemv<<<grid, 32, sizeof(float) * GV_STAGES * GV_STAGE_FLOATS, s>>>(pb);
+    return;
+  }
+  // Most independent chains per thread that still gives every SM sub-partition
+  // (148 SMs x 4) a warp; else the finest tile.
+  const long panels = (max_m + 31) / 32;
+  auto warps = [&](int bn, int threads) { return panels * ((max_b + bn - 1) / bn) * (threads / 32) * pb.count; };
+  const long want = 148 * 4;
+  // NEUROGEN_PROJ_TILE = 8 | 16 | 32 | 64 forces one session tile (tests of
+  // every tile shape); results do not depend on the tile.
+  static const int forced = [] {
+    const char *v = std::getenv("NEUROGEN_PROJ_TILE");
+    return v ? std::atoi(v) : 0;
+  }();
+  switch (forced) {
+  case 8: return run_gemm<8, 1>(pb, max_m, max_b, s);
+  case 16: return run_gemm<16, 2>(pb, max_m, max_b, s);
+  case 32: return run_gemm<32, 4>(pb, max_m, max_b, s);
+  case 64: return run_gemm<64, 4>(pb, max_m, max_b, s);
+  default: break;
+  }
+  if (max_b > 32 && warps(64, gemm_threads<64, 4>()) >= want) run_gemm<64, 4>(pb, max_m, max_b, s);
+  else if (max_b > 16 && warps(32, gemm_threads<32, 4>()) >= want) run_gemm<32, 4>(pb, max_m, max_b, s);
+  else if (max_b > 8 && warps(16, gemm_threads<16, 2>()) >= want) run_gemm<16, 2>(pb, max_m, max_b, s);
+  else run_gemm<8, 1>(pb, max_m, max_b, s);
 }
 
 void launch_projection(const ProjArgs &a, cudaStream_t s) {
-  if (a.B <= 0 || a.M <= 0) return;
-  if (a.B == 1) {
-    dim3 grid((a.M + 31) / 32, 1);
-    k_gemv<<<grid, 32, 0, s>>>(a);
-    return;
-  }
-  // Smallest session tile that still gives every SM a CTA, else the widest.
-  const long mt = (a.M + GM_BM - 1) / GM_BM;
-  const int sms = 148;
-  if (a.B <= 16 || mt * ((a.B + 31) / 32) < sms) run_gemm<16, 1>(a, s);
-  else if (mt * ((a.B + 63) / 64) < sms) run_gemm<32, 2>(a, s);
-  else run_gemm<64, 4>(a, s);
+  ProjBatch pb{};
+  pb.a[0] = a;
+  pb.count = 1;
+  launch_projections(pb, s);
 }
 
 void launch_tick(const TickArgs &a, cudaStream_t s) {

@@ -34,6 +34,12 @@ struct ProjArgs {
   int M, K, B;
 };
 void launch_projection(const ProjArgs &a, cudaStream_t s);
+// Up to 4 independent projections (e.g. every region's feedback) in one launch.
+struct ProjBatch {
+  ProjArgs a[4];
+  int count;
+};
+void launch_projections(const ProjBatch &pb, cudaStream_t s);
 // Per-device kernel attributes (dynamic shared memory); call once per device
 // before launching, outside any stream capture.
 void configure_lang_kernels();

@@ -516,24 +516,18 @@ Network::Network(const Topology &topo) : cfg(topo.cfg) {
   d.drive_thr = thr >= 4294967295.0 ? 0xFFFFFFFFu : uint32_t(thr);
   d.drive_key = mix64(c.seed ^ 0xD41Eull);
   d.ref_ticks = int(std::lround(double(c.t_ref_ms) / double(c.dt_ms)));
-  // Work list, its two counters, the current bitmask and the running totals.
-  const size_t words = (N + 31) / 32;
-  active_.reset(std::max<size_t>(N, 1) * sizeof(int2));
-  nact_.reset(2 * sizeof(unsigned));
-  bitmask_.reset(words * 4);
-  totals_.reset(2 * sizeof(unsigned long long));
+  // Current bitmask (padded to whole 256-neuron groups), per-group totals, tick.
+  const size_t groups = (N + kNetBlock - 1) / kNetBlock;
+  bitmask_.reset(groups * (kNetBlock / 32) * 4);
+  totals_.reset(groups * 2 * sizeof(unsigned long long));
   tick_dev_.reset(sizeof(long long));
-  NGB_CUDA(cudaMemset(nact_.as<void>(), 0, 2 * sizeof(unsigned)));
-  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, words * 4));
-  NGB_CUDA(cudaMemset(totals_.as<void>(), 0, 2 * sizeof(unsigned long long)));
+  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, groups * (kNetBlock / 32) * 4));
+  NGB_CUDA(cudaMemset(totals_.as<void>(), 0, groups * 2 * sizeof(unsigned long long)));
   NGB_CUDA(cudaMemset(tick_dev_.as<void>(), 0, sizeof(long long)));
-  d.active = active_.as<int2>();
-  d.nact = nact_.as<unsigned>();
   d.bitmask = bitmask_.as<uint32_t>();
   d.totals = totals_.as<unsigned long long>();
   // Small networks: one fused launch per tick; large: split membrane / push.
   split_ = c.launch == 2 || (c.launch == 0 && n_ >= 65536);
-  push_blocks_ = net_push_blocks(d);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
 }
 
@@ -545,7 +539,7 @@ Network::~Network() {
 void Network::launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st) {
   if (split_) {
     launch_net_alif(dev_, t, spikes_row, counts_row, st);
-    launch_net_push(dev_, t, counts_row, push_blocks_, st);
+    launch_net_push(dev_, t, counts_row, st);
   } else {
     launch_net_fused(dev_, t, spikes_row, counts_row, st);
   }
@@ -572,7 +566,14 @@ void Network::capture_graph() {
 void Network::stats(int64_t *totals) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaDeviceSynchronize());
-  NGB_CUDA(cudaMemcpy(totals, totals_.as<void>(), 16, cudaMemcpyDeviceToHost));
+  const size_t groups = (size_t(n_) + kNetBlock - 1) / kNetBlock;
+  std::vector<unsigned long long> g(groups * 2);
+  NGB_CUDA(cudaMemcpy(g.data(), totals_.as<void>(), g.size() * 8, cudaMemcpyDeviceToHost));
+  totals[0] = totals[1] = 0;
+  for (size_t k = 0; k < groups; ++k) {
+    totals[0] += int64_t(g[2 * k]);
+    totals[1] += int64_t(g[2 * k + 1]);
+  }
 }
 
 void Network::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *weight) {
@@ -622,7 +623,6 @@ void Network::set_state(const float *v, const float *a, const float *ge, const f
   if (ref) NGB_CUDA(cudaMemcpy(ref_.as<void>(), ref, N * 4, cudaMemcpyHostToDevice));
   if (ring) NGB_CUDA(cudaMemcpy(ring_.as<void>(), ring, size_t(kRingSlots) * N * 8, cudaMemcpyHostToDevice));
   if (tick < 0) throw std::invalid_argument("tick must be non-negative");
-  NGB_CUDA(cudaMemset(nact_.as<void>(), 0, 2 * sizeof(unsigned)));
   tick_ = tick;
 }
 

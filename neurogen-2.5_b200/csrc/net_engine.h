@@ -83,9 +83,8 @@ private:
   DeviceBuffer row_, syn_, w_, outdeg_, bcol_, blk_, tiles_;
   DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
   DeviceBuffer rec_spikes_, rec_counts_;
-  DeviceBuffer active_, nact_, bitmask_, totals_, tick_dev_;
+  DeviceBuffer bitmask_, totals_, tick_dev_;
   bool split_ = false;
-  int push_blocks_ = 0;
   cudaGraphExec_t graph_ = nullptr;
   static constexpr int kGraphTicks = 64;
   void launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st);

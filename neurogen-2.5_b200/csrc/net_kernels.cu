@@ -11,12 +11,14 @@
 // Two launch shapes, identical arithmetic:
 //   fused  -- one kernel per tick; the warp that owns a spiking neuron pushes
 //             its synapses.  Cheapest for small networks (one launch).
-//   split  -- k_net_alif appends spiking neurons (CSR) or active 16-neuron
-//             block-columns (block storage) to a work list with one atomic per
-//             CTA, then a persistent k_net_push_* grid gives every warp one
-//             list item at a time with all of a lane's synapse loads in flight
-//             before its deliveries.  For large networks, where the push is a
-//             bandwidth problem.
+//   split  -- k_net_alif updates the neurons and writes the bitmask; then
+//             k_net_push CTA b reads the 8 bitmask words of neuron group b,
+//             lists its spiking neurons (CSR) or non-empty 16-neuron
+//             block-columns (block storage) in shared memory, and its 8 warps
+//             take the items round-robin, each lane with all of its synapse
+//             loads in flight before its deliveries.  For large networks.
+// Spike and event counts accumulate into one counter pair per 256-neuron
+// group, so the hot path has no same-address atomics.
 //
 // Numerics contract (shared with the C oracle, oracle/net_oracle.c): fp32
 // state, every operation rounded as written (__f*_rn intrinsics, -fmad=false),
@@ -195,9 +197,10 @@ __device__ __forceinline__ void push_block_column(const NetDev &d, long long t, 
   }
 }
 
-// CTA-wide sum of one value per warp (lane 0 contributes), added once to the
-// running total and, when given, to this tick's counter.
-__device__ __forceinline__ void add_block_count(unsigned long long v, unsigned long long *total,
+// CTA-wide sum of one value per warp (lane 0 contributes), added to this
+// group's running counter (single writer) and, when given, to this tick's
+// counter (recording runs only).
+__device__ __forceinline__ void add_block_count(unsigned long long v, unsigned long long *group_total,
                                                 unsigned long long *tick_count) {
   __shared__ unsigned long long part[WARPS];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -208,10 +211,8 @@ __device__ __forceinline__ void add_block_count(unsigned long long v, unsigned l
   if (threadIdx.x == 0) {
     unsigned long long s = 0;
     for (int k = 0; k < WARPS; ++k) s += part[k];
-    if (s) {
-      atomicAdd(total, s);
-      if (tick_count) atomicAdd(tick_count, s);
-    }
+    *group_total += s;
+    if (tick_count && s) atomicAdd(tick_count, s);
   }
   __syncthreads();
 }
@@ -245,19 +246,17 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
     }
   }
   if (s) events = (unsigned long long)d.outdeg[i];
-  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals, counts);
-  add_block_count(events, d.totals + 1, counts ? counts + 1 : nullptr);
+  unsigned long long *group = d.totals + 2 * (size_t)blockIdx.x;
+  add_block_count(lane == 0 ? __popc(fired) : 0, group, counts);
+  add_block_count(events, group + 1, counts ? counts + 1 : nullptr);
 }
 
 template <bool BSR>
 __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t *spikes_out,
                                                  unsigned long long *counts) {
-  __shared__ unsigned warp_items[WARPS];
-  __shared__ unsigned block_base;
   const long long t = tick_of(tr);
-  const int par = (int)(t & 1);
   const int i = blockIdx.x * TB + threadIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const bool s = i < d.n ? alif_update(d, t, i) : false;
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
@@ -265,54 +264,68 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
     d.bitmask[base >> 5] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
-  // Work items of this warp: its spiking neurons, or its non-empty halves.
-  const unsigned sub0 = fired & 0xFFFFu, sub1 = fired >> 16;
-  const unsigned items = BSR ? (unsigned)(sub0 != 0) + (unsigned)(sub1 != 0) : (unsigned)__popc(fired);
-  if (lane == 0) warp_items[warp] = items;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned total = 0;
-    for (int k = 0; k < WARPS; ++k) {
-      const unsigned c = warp_items[k];
-      warp_items[k] = total;
-      total += c;
-    }
-    block_base = total ? atomicAdd(d.nact + par, total) : 0;
-  }
-  __syncthreads();
-  const unsigned at = block_base + warp_items[warp];
-  if (BSR) {
-    if (lane == 0) {
-      unsigned k = at;
-      if (sub0) d.active[k++] = make_int2(base >> 4, (int)sub0);
-      if (sub1) d.active[k] = make_int2((base >> 4) + 1, (int)sub1);
-    }
-  } else if (s) {
-    d.active[at + __popc(fired & ((1u << lane) - 1u))] = make_int2(i, 0);
-  }
-  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals, counts);
+  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + 2 * (size_t)blockIdx.x, counts);
 }
 
+// CTA b pushes the spikes of neurons [256b, 256b+256): its warps list them
+// from the group's 8 bitmask words and take them round-robin.
 template <bool BSR>
 __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned long long *counts) {
+  __shared__ int items[TB];
+  __shared__ unsigned item_mask[TB / 16];
+  __shared__ int n_items;
   const long long t = tick_of(tr);
-  const int par = (int)(t & 1);
-  const int lane = threadIdx.x & 31;
-  const unsigned n_act = d.nact[par];
-  if (blockIdx.x == 0 && threadIdx.x == 0) d.nact[par ^ 1] = 0; // next tick's list starts empty
-  const unsigned stride = gridDim.x * WARPS;
-  unsigned long long events = 0;
-  for (unsigned a = blockIdx.x * WARPS + (threadIdx.x >> 5); a < n_act; a += stride) {
-    const int2 item = d.active[a];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = blockIdx.x * TB;
+  if (warp == 0) {
+    const int w = base / 32 + (lane & 7);
+    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n) ? d.bitmask[w] : 0u;
     if (BSR) {
-      push_block_column(d, t, item.x, (unsigned)item.y, lane);
-      if (lane < 16 && ((unsigned)item.y >> lane & 1u)) events += (unsigned long long)d.outdeg[item.x * 16 + lane];
+      // 16 block-columns per group; lane k < 16 owns half (k & 1) of word k / 2.
+      const unsigned wk = __shfl_sync(0xffffffffu, word, (lane >> 1) & 7);
+      const unsigned sub = lane < 16 ? ((wk >> (16 * (lane & 1))) & 0xFFFFu) : 0u;
+      const unsigned has = __ballot_sync(0xffffffffu, sub != 0);
+      if (sub) {
+        const int at = __popc(has & ((1u << lane) - 1u));
+        items[at] = (base >> 4) + lane;
+        item_mask[at] = sub;
+      }
+      if (lane == 0) n_items = __popc(has);
     } else {
-      push_row(d, t, item.x, lane);
-      if (lane == 0) events += (unsigned long long)d.outdeg[item.x];
+      const unsigned cnt = lane < WARPS ? __popc(word) : 0u;
+      unsigned pre = cnt; // inclusive scan over the 8 words
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += v;
+      }
+      if (lane < WARPS) {
+        unsigned m = word, at = pre - cnt;
+        while (m) {
+          const int b = __ffs(m) - 1;
+          m &= m - 1;
+          items[at++] = base + lane * 32 + b;
+        }
+      }
+      if (lane == WARPS - 1) n_items = (int)pre;
     }
   }
-  add_block_count(events, d.totals + 1, counts ? counts + 1 : nullptr);
+  __syncthreads();
+  const int count = n_items;
+  unsigned long long events = 0;
+  for (int k = warp; k < count; k += WARPS) {
+    if (BSR) {
+      const int bc = items[k];
+      const unsigned sub = item_mask[k];
+      push_block_column(d, t, bc, sub, lane);
+      if (lane < 16 && (sub >> lane & 1u)) events += (unsigned long long)d.outdeg[bc * 16 + lane];
+    } else {
+      const int pre = items[k];
+      push_row(d, t, pre, lane);
+      if (lane == 0) events += (unsigned long long)d.outdeg[pre];
+    }
+  }
+  add_block_count(events, d.totals + 2 * (size_t)blockIdx.x + 1, counts ? counts + 1 : nullptr);
 }
 
 __global__ void k_set_tick(long long *t, long long v) { *t = v; }
@@ -334,18 +347,10 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
   else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
 }
 
-void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int push_blocks, cudaStream_t s) {
-  if (d.bsr) k_net_push<true><<<push_blocks, TB, 0, s>>>(d, t, counts);
-  else k_net_push<false><<<push_blocks, TB, 0, s>>>(d, t, counts);
-}
-
-int net_push_blocks(const NetDev &d) {
-  int dev = 0, sms = 0, per = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (d.bsr) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_net_push<true>, TB, 0);
-  else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_net_push<false>, TB, 0);
-  return sms * (per > 0 ? per : 1);
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, cudaStream_t s) {
+  const int blocks = (d.n + TB - 1) / TB;
+  if (d.bsr) k_net_push<true><<<blocks, TB, 0, s>>>(d, t, counts);
+  else k_net_push<false><<<blocks, TB, 0, s>>>(d, t, counts);
 }
 
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s) { k_set_tick<<<1, 1, 0, s>>>(t_dev, value); }

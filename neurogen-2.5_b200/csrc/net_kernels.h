@@ -30,13 +30,10 @@ struct NetDev {
   float *v, *a, *ge, *gi;
   int *ref;
   int2 *ring;
-  // Per-tick work list of the split path: spiking neurons (CSR) or
-  // (block-column, 16-bit spike mask) pairs (blocks), with two counters used
-  // alternately by even and odd ticks.
-  int2 *active;
-  unsigned *nact;               // [2]
   uint32_t *bitmask;            // this tick's spike words [ceil(n/32)]
-  unsigned long long *totals;   // [2] spikes, synaptic events since creation
+  // Running (spikes, synaptic events) of each membrane CTA's 256 neurons since
+  // creation, [ceil(n/256)][2]; each entry has one writer, so no atomics.
+  unsigned long long *totals;
   // Constants (see net_kernels.cu for the exact operation order).
   float dE, dI, dA, g_leak, gLEL, e_inh, v_th, v_reset, cap_e, cap_i, neg_dt, adapt_inc, bias,
       drive_ns;
@@ -56,12 +53,12 @@ struct TickRef {
 // Fused single launch per tick (small networks): ALIF, ballot, push.
 void launch_net_fused(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
                       cudaStream_t s);
-// Split path (large networks): ALIF + bitmask + work list, then the push.
+// Split path (large networks): ALIF + bitmask, then the push of the spikes of
+// each 256-neuron group by one CTA.
 void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
                      cudaStream_t s);
-void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int push_blocks,
-                     cudaStream_t s);
-int net_push_blocks(const NetDev &d); // persistent grid size of the push kernel
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, cudaStream_t s);
+constexpr int kNetBlock = 256; // neurons per membrane CTA
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s);
 void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s);
 

@@ -221,3 +221,35 @@ def test_pool_matches_host_batch():
         assert np.array_equal(lb, logits) and np.array_equal(sb, st)
     finally:
         lib.ng_pool_destroy(pool)
+
+
+@pytest.mark.parametrize('tile', ['8', '16', '32', '64'])
+def test_every_projection_tile_is_bit_identical(tile):
+    """Each session tile of the batched projection gives the same bits as the batch-1 kernel
+    (one sequential chain per output in every case).  Runs in a child process because the
+    tile override is read once per process."""
+    import os
+    import subprocess
+    import sys
+    code = f"""
+import sys, numpy as np
+sys.path[:0] = {[str(p) for p in sys.path[:3]]!r}
+from neurogen_b200.language import LanguageConfig, NativeEngine, init_packed_weights
+cfg = LanguageConfig(columns=6, width=96, regions=3, ticks=2, idle_steps=1)
+eng = NativeEngine(cfg, init_packed_weights(cfg, seed=11))
+B = 45
+rng = np.random.default_rng(1)
+toks = rng.integers(0, 264, (3, B))
+sb = np.zeros((B, eng.state_size), np.float32)
+single = np.zeros((B, eng.state_size), np.float32)
+for t in range(3):
+    lb, sb, _, _ = eng.step_batch(toks[t], sb)
+    for b in (0, 7, 44):
+        l1, s1, _, _ = eng.step_batch(toks[t, b:b + 1], single[b:b + 1])
+        single[b] = s1[0]
+        assert np.array_equal(l1[0], lb[b]) and np.array_equal(s1[0], sb[b]), (t, b)
+print('ok')
+"""
+    env = dict(os.environ, NEUROGEN_PROJ_TILE=tile)
+    out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and 'ok' in out.stdout, out.stderr[-2000:]
