@@ -74,6 +74,21 @@ int ng_advance_batch(void *engine, const float *inputs, int batch,
                      const float *state, size_t state_count, int idle,
                      float *next_state, float *hidden, float *activity);
 
+/* Same as ng_step, but it allocates no device memory of its own: the state
+ * staging, the activations between kernels and the outputs live in a fixed
+ * 1 MiB array compiled into this library (every GPU that loads the library
+ * holds it until exit).  No counterpart in the reference.  For callers that
+ * cannot have a step allocate -- a fixed device-memory budget, or a streaming
+ * loop where a cudaMalloc could block on the driver's allocation lock and
+ * synchronise the device.  Models whose step needs more than 262,144 floats
+ * of working memory are rejected with an error (BC-250 needs ~57k).  The
+ * first call on a device looks the array up and loads the kernels; make it
+ * before any stream capture.  Calls share the array: this process serialises
+ * them, and calls that overlap on the GPU from other means would race. */
+int ng_step_static(void *engine, int token, const float *state,
+                   size_t state_count, float *next_state, float *logits,
+                   float *hidden, float *activity);
+
 /* ------------------------------------------------------------------------ */
 /* Part 3: device-resident session pools (state stays in HBM between calls). */
 /* ------------------------------------------------------------------------ */

@@ -181,12 +181,12 @@ DeviceModel::~DeviceModel() {
   if (stream) cudaStreamDestroy(stream);
 }
 
-void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, bool first_idle,
-                          int advances, float *d_state, float *d_logits, float *d_hidden,
-                          float *d_act, Scratch &sc, cudaStream_t st) const {
+void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs, bool first_idle,
+                               int advances, float *d_state, float *d_logits, float *d_hidden,
+                               float *d_act, const ScratchView &sc, cudaStream_t st) const {
   const LangDims &d = dims;
   const int A = advances;
-  NGB_CUDA(cudaMemsetAsync(sc.cnt.as<int>(), 0, size_t(B) * A * d.R * sizeof(int), st));
+  NGB_CUDA(cudaMemsetAsync(sc.cnt, 0, size_t(B) * A * d.R * sizeof(int), st));
   const int Min = d.c * d.n_in, Mfb = d.c * d.n_fb, Kout = d.c * d.n_out * 2;
   for (int adv = 0; adv < A; ++adv) {
     const bool idle = adv > 0 || first_idle;
@@ -202,7 +202,7 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
         fa.wp = regions[r].fb_wp.as<float>();
         fa.x = d_state + r * d.RS + 4L * d.n;
         fa.ldx = d.S;
-        fa.y = sc.fb.as<float>() + size_t(r) * B * Mfb;
+        fa.y = sc.fb + size_t(r) * B * Mfb;
         fa.ldy = Mfb;
         fa.M = Mfb;
         fa.K = d.w;
@@ -222,10 +222,10 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
           ia.x = d_tokens ? emb.as<float>() : d_inputs;
           ia.xidx = d_tokens;
         } else {
-          ia.x = sc.h.as<float>();
+          ia.x = sc.h;
         }
         ia.ldx = d.w;
-        ia.y = sc.vin.as<float>();
+        ia.y = sc.vin;
         ia.ldy = Min;
         ia.M = Min;
         ia.K = d.w;
@@ -246,30 +246,30 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
         if (t % 2 == 0) {
           ta.tr_in = state_trace;
           ta.tr_in_ld = d.S;
-          ta.tr_out = sc.tr.as<float>();
+          ta.tr_out = sc.tr;
           ta.tr_out_ld = d.n;
         } else {
-          ta.tr_in = sc.tr.as<float>();
+          ta.tr_in = sc.tr;
           ta.tr_in_ld = d.n;
           ta.tr_out = state_trace;
           ta.tr_out_ld = d.S;
         }
-        ta.vin = sensory ? sc.vin.as<float>() : nullptr;
-        ta.fb = sc.fb.as<float>() + size_t(r) * B * Mfb;
-        ta.feat = t == d.T - 1 ? sc.feat.as<float>() : nullptr;
-        ta.spikes = sc.cnt.as<int>() + adv * d.R + r;
+        ta.vin = sensory ? sc.vin : nullptr;
+        ta.fb = sc.fb + size_t(r) * B * Mfb;
+        ta.feat = t == d.T - 1 ? sc.feat : nullptr;
+        ta.spikes = sc.cnt + adv * d.R + r;
         ta.spikes_ld = long(A) * d.R;
         ta.tab = tables;
         launch_tick(ta, st);
       }
       if (d.T % 2 == 1)
-        launch_copy_rows(sc.tr.as<float>(), d.n, d_state + roff + d.n, d.S, d.n, B, st);
+        launch_copy_rows(sc.tr, d.n, d_state + roff + d.n, d.S, d.n, B, st);
       ProjArgs oa{};
       oa.wp = g.out_wp.as<float>();
       oa.bias = g.out_b.as<float>();
-      oa.x = sc.feat.as<float>();
+      oa.x = sc.feat;
       oa.ldx = Kout;
-      oa.y = sc.hraw.as<float>();
+      oa.y = sc.hraw;
       oa.ldy = d.w;
       oa.addv = d_state + roff + 4L * d.n; // memory before this region's update
       oa.ldadd = d.S;
@@ -278,9 +278,9 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
       oa.B = B;
       launch_projection(oa, st);
       NormArgs na{};
-      na.hraw = sc.hraw.as<float>();
+      na.hraw = sc.hraw;
       na.hraw_ld = d.w;
-      na.h = sc.h.as<float>();
+      na.h = sc.h;
       na.h_ld = d.w;
       na.mem = d_state + roff + 4L * d.n;
       na.mem_ld = d.S;
@@ -296,7 +296,7 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
     ProjArgs ha{};
     ha.wp = head_wp.as<float>();
     ha.bias = head_b.as<float>();
-    ha.x = sc.h.as<float>();
+    ha.x = sc.h;
     ha.ldx = d.w;
     ha.y = d_logits;
     ha.ldy = kVocab;
@@ -306,8 +306,8 @@ void DeviceModel::enqueue(int B, const int *d_tokens, const float *d_inputs, boo
     launch_projection(ha, st);
   }
   if (d_hidden)
-    NGB_CUDA(cudaMemcpyAsync(d_hidden, sc.h.as<float>(), size_t(B) * d.w * 4, cudaMemcpyDeviceToDevice, st));
-  if (d_act) launch_activity(sc.cnt.as<int>(), A, d.R, d.n, d.T, d_act, B, st);
+    NGB_CUDA(cudaMemcpyAsync(d_hidden, sc.h, size_t(B) * d.w * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_act) launch_activity(sc.cnt, A, d.R, d.n, d.T, d_act, B, st);
   NGB_CUDA(cudaGetLastError());
 }
 

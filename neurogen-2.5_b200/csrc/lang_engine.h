@@ -29,11 +29,23 @@ struct RegionWeights {
   DeviceBuffer norm_w, norm_b, decay;   // [w]
 };
 
+// Device working memory one token step / advance needs, as raw pointers
+// (sizes for B sessions: h, hraw [B][w]; vin [B][c*n_in]; fb [R][B][c*n_fb];
+// tr [B][n]; feat [B][c*n_out*2]; cnt int [B][1+idle][R]).
+struct ScratchView {
+  float *h, *hraw, *vin, *fb, *tr, *feat;
+  int *cnt;
+};
+
 // Per-call device workspace for `capacity` sessions.
 struct Scratch {
   int capacity = 0;
   DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act;
   void ensure(const LangDims &d, int batch);
+  ScratchView view() const {
+    return {h.as<float>(), hraw.as<float>(), vin.as<float>(), fb.as<float>(),
+            tr.as<float>(), feat.as<float>(), cnt.as<int>()};
+  }
 };
 
 class DeviceModel {
@@ -50,7 +62,13 @@ public:
   // first_idle is set.  Outputs may be null.
   void enqueue(int B, const int *d_tokens, const float *d_inputs, bool first_idle, int advances,
                float *d_state, float *d_logits, float *d_hidden, float *d_act, Scratch &sc,
-               cudaStream_t st) const;
+               cudaStream_t st) const {
+    enqueue_view(B, d_tokens, d_inputs, first_idle, advances, d_state, d_logits, d_hidden, d_act, sc.view(), st);
+  }
+  // The same launch sequence on caller-provided working memory.
+  void enqueue_view(int B, const int *d_tokens, const float *d_inputs, bool first_idle, int advances,
+                    float *d_state, float *d_logits, float *d_hidden, float *d_act, const ScratchView &sc,
+                    cudaStream_t st) const;
 
   LangDims dims;
   int device = 0;

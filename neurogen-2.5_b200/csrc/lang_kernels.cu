@@ -381,6 +381,20 @@ void configure_lang_kernels() {
                        (int)(sizeof(float) * GV_STAGES * GV_STAGE_FLOATS));
 }
 
+void preload_lang_kernels() {
+  cudaFuncAttributes fa;
+  const void *kernels[] = {(const void *)k_gemv,
+                           (const void *)k_gemm<8, 1>,
+                           (const void *)k_gemm<16, 2>,
+                           (const void *)k_gemm<32, 4>,
+                           (const void *)k_gemm<64, 4>,
+                           (const void *)k_tick,
+                           (const void *)k_copy_rows,
+                           (const void *)k_norm,
+                           (const void *)k_activity};
+  for (const void *k : kernels) cudaFuncGetAttributes(&fa, k);
+}
+
 void launch_projections(const ProjBatch &pb, cudaStream_t s) {
   int max_m = 0, max_b = 0;
   for (int z = 0; z < pb.count; ++z) {

@@ -43,6 +43,9 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s);
 // Per-device kernel attributes (dynamic shared memory); call once per device
 // before launching, outside any stream capture.
 void configure_lang_kernels();
+// Forces every language-core kernel to be loaded on the current device now
+// (under lazy module loading a first launch would otherwise load it).
+void preload_lang_kernels();
 
 // One synchronous recurrent ALIF tick of one region for B sessions
 // (reference CPUBackend.cpp:20-42 with the input current assembled as in
