@@ -232,38 +232,35 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
         ia.B = B;
         launch_projection(ia, st);
       }
-      for (int t = 0; t < d.T; ++t) {
-        TickArgs ta{};
-        ta.rec = g.rec.as<float>();
-        ta.state = d_state;
-        ta.S = d.S;
-        ta.roff = roff;
-        ta.n = d.n;
-        ta.c = d.c;
-        ta.w = d.w;
-        ta.B = B;
+      TickArgs ta{};
+      ta.rec = g.rec.as<float>();
+      ta.state = d_state;
+      ta.S = d.S;
+      ta.roff = roff;
+      ta.n = d.n;
+      ta.c = d.c;
+      ta.w = d.w;
+      ta.B = B;
+      ta.vin = sensory ? sc.vin : nullptr;
+      ta.fb = sc.fb + size_t(r) * B * Mfb;
+      ta.spikes = sc.cnt + adv * d.R + r;
+      ta.spikes_ld = long(A) * d.R;
+      ta.tab = tables;
+      ta.feat = sc.feat;
+      if (!launch_ticks_cluster(ta, d.T, st)) {
+        // No cluster shape for this column count: one launch per tick with a
+        // ping-pong trace buffer, then the trace back into the state.
         float *state_trace = d_state + roff + d.n;
-        if (t % 2 == 0) {
-          ta.tr_in = state_trace;
-          ta.tr_in_ld = d.S;
-          ta.tr_out = sc.tr;
-          ta.tr_out_ld = d.n;
-        } else {
-          ta.tr_in = sc.tr;
-          ta.tr_in_ld = d.n;
-          ta.tr_out = state_trace;
-          ta.tr_out_ld = d.S;
+        for (int t = 0; t < d.T; ++t) {
+          ta.tr_in = t % 2 == 0 ? state_trace : sc.tr;
+          ta.tr_in_ld = t % 2 == 0 ? d.S : d.n;
+          ta.tr_out = t % 2 == 0 ? sc.tr : state_trace;
+          ta.tr_out_ld = t % 2 == 0 ? d.n : d.S;
+          ta.feat = t == d.T - 1 ? sc.feat : nullptr;
+          launch_tick(ta, st);
         }
-        ta.vin = sensory ? sc.vin : nullptr;
-        ta.fb = sc.fb + size_t(r) * B * Mfb;
-        ta.feat = t == d.T - 1 ? sc.feat : nullptr;
-        ta.spikes = sc.cnt + adv * d.R + r;
-        ta.spikes_ld = long(A) * d.R;
-        ta.tab = tables;
-        launch_tick(ta, st);
+        if (d.T % 2 == 1) launch_copy_rows(sc.tr, d.n, state_trace, d.S, d.n, B, st);
       }
-      if (d.T % 2 == 1)
-        launch_copy_rows(sc.tr, d.n, d_state + roff + d.n, d.S, d.n, B, st);
       ProjArgs oa{};
       oa.wp = g.out_wp.as<float>();
       oa.bias = g.out_b.as<float>();

@@ -20,9 +20,14 @@
 // result differs by an ulp; the parity tests quantify that.
 #include "lang_kernels.h"
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstdlib>
+#include <stdexcept>
+#include <string>
+
+namespace cg = cooperative_groups;
 
 namespace ngb {
 namespace {
@@ -106,8 +111,16 @@ __global__ void __launch_bounds__(32) k_gemv(ProjBatch pb) {
     if (lane < GV_ROWS) {
       const int kc = min(GV_KC, a.K - ch * GV_KC);
       if (kc == GV_KC) {
+        // 16 independent products, then their 16 dependent adds: operand
+        // loads and multiplies of the next group overlap this group's chain.
 #pragma unroll
-        for (int k = 0; k < GV_KC; ++k) acc = __fadd_rn(acc, __fmul_rn(ws[k * GV_ROWS + lane], xs[k]));
+        for (int g = 0; g < GV_KC; g += 16) {
+          float pr[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pr[j] = __fmul_rn(ws[(g + j) * GV_ROWS + lane], xs[g + j]);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, pr[j]);
+        }
       } else {
         for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(ws[k * GV_ROWS + lane], xs[k]));
       }
@@ -147,6 +160,28 @@ __device__ __forceinline__ void load_x(const float *p, float (&x)[TN]) {
   for (int s = 0; s < TN; ++s) x[s] = f[s];
 }
 
+// Packed pairs of fp32 (sm_100 f32x2): each lane of a .f32x2 op is one IEEE
+// round-to-nearest fp32 op, so pairing two independent chains changes no bit.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(f32x2 v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 template <int BN, int TN>
 __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
   constexpr int NT = gemm_threads<BN, TN>(), STAGE = gemm_stage_floats<BN>();
@@ -172,13 +207,20 @@ __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
   };
 #pragma unroll
   for (int s = 0; s < GM_STAGES - 1; ++s) issue(s);
-  float acc[4][TN];
+  // acc[h][s]: rows (4tx + 2h, 4tx + 2h + 1) of session ty*TN + s.
+  f32x2 acc[2][TN];
+  {
+    float init[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = p * 32 + tx * 4 + i;
-    const float init = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const int m = p * 32 + tx * 4 + i;
+      init[i] = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+    }
 #pragma unroll
-    for (int s = 0; s < TN; ++s) acc[i][s] = init;
+    for (int s = 0; s < TN; ++s) {
+      acc[0][s] = pack2(init[0], init[1]);
+      acc[1][s] = pack2(init[2], init[3]);
+    }
   }
   for (int ch = 0; ch < nch; ++ch) {
     issue(ch + GM_STAGES - 1);
@@ -189,13 +231,21 @@ __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
     const int kc = min(GM_KC, a.K - ch * GM_KC);
     auto step = [&](int k) {
       const float4 wv = *reinterpret_cast<const float4 *>(ws + k * 32 + tx * 4);
-      const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
+      const f32x2 w01 = pack2(wv.x, wv.y), w23 = pack2(wv.z, wv.w);
       float xr[TN];
       load_x<TN>(xs + k * BN + ty * TN, xr);
+      f32x2 pr[2][TN];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int s = 0; s < TN; ++s) {
+        const f32x2 xx = pack2(xr[s], xr[s]);
+        pr[0][s] = mul2(w01, xx);
+        pr[1][s] = mul2(w23, xx);
+      }
 #pragma unroll
-        for (int s = 0; s < TN; ++s) acc[i][s] = __fadd_rn(acc[i][s], __fmul_rn(w4[i], xr[s]));
+      for (int s = 0; s < TN; ++s) {
+        acc[0][s] = add2(acc[0][s], pr[0][s]);
+        acc[1][s] = add2(acc[1][s], pr[1][s]);
+      }
     };
     if (kc == GM_KC) {
 #pragma unroll
@@ -206,13 +256,16 @@ __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = p * 32 + tx * 4 + i;
+  for (int s = 0; s < TN; ++s) {
+    float r[4];
+    unpack2(acc[0][s], r[0], r[1]);
+    unpack2(acc[1][s], r[2], r[3]);
+    const int b = b0 + ty * TN + s;
 #pragma unroll
-    for (int s = 0; s < TN; ++s) {
-      const int b = b0 + ty * TN + s;
+    for (int i = 0; i < 4; ++i) {
+      const int m = p * 32 + tx * 4 + i;
       if (m < a.M && b < a.B) {
-        float v = acc[i][s];
+        float v = r[i];
         if (a.addv) v = __fadd_rn(v, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
         a.y[(long)b * a.ldy + m] = v;
       }
@@ -303,6 +356,117 @@ __global__ void __launch_bounds__(64 * TK_SB) k_tick(TickArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// All ticks of one region in one launch: a thread-block cluster of CL CTAs
+// covers the region's c columns (CPC = c / CL each, weights in shared memory).
+// Unit state stays in registers across ticks; each tick's traces go to a
+// shared-memory ping-pong buffer, and the excitatory neighbour term reads the
+// adjacent CTA's edge column through distributed shared memory after a
+// cluster barrier.  Same arithmetic as k_tick, tick for tick.
+// ---------------------------------------------------------------------------
+template <int CPC, int SB>
+__global__ void __launch_bounds__(64 * CPC * SB) k_ticks_cluster(TickArgs a, int ticks) {
+  extern __shared__ __align__(16) float tsm[];
+  float *wt = tsm;                              // [CPC][64][TK_LD]
+  float *trb = tsm + CPC * 64 * TK_LD;          // [2][SB][CPC][64]
+  cg::cluster_group cluster = cg::this_cluster();
+  const int g = blockIdx.x;                     // column group = rank in the cluster
+  const int tid = threadIdx.x, id = tid & 63, cl = (tid >> 6) % CPC, s = tid / (64 * CPC);
+  const int col = g * CPC + cl, b = blockIdx.y * SB + s;
+  const bool live = b < a.B;
+  for (int i = tid; i < CPC * 4096; i += 64 * CPC * SB) {
+    const int c = i >> 12, r = i & 4095;
+    wt[c * 64 * TK_LD + (r >> 6) * TK_LD + (r & 63)] = a.rec[(size_t)(g * CPC + c) * 4096 + r];
+  }
+  const bool exc = (a.tab.exc_mask >> id) & 1ull;
+  const int n = a.n, i = col * 64 + id;
+  float *st = a.state + (long)(live ? b : 0) * a.S + a.roff;
+  float V = 0.f, adapt = 0.f, last = 0.f, cnt = 0.f, trace = 0.f, current = 0.f;
+  if (live) {
+    V = st[i];
+    trace = st[n + i];
+    adapt = st[2 * n + i];
+    last = st[3 * n + i];
+    cnt = st[4 * n + a.w + i];
+    current = exc ? .15f : .35f;
+    const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
+    if (a.vin && ii >= 0) current = 3 * host_sigmoid(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii]);
+    if (fi >= 0) current = current + .5f * host_tanh(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi]);
+  }
+  auto tr_at = [&](int buf, int ss, int cc) { return trb + ((buf * SB + ss) * CPC + cc) * 64; };
+  tr_at(0, s, cl)[id] = trace;
+  cluster.sync();
+  const float decay = exc ? .6f : .4f;
+  const float *wr = wt + cl * 64 * TK_LD + id * TK_LD;
+  for (int t = 0; t < ticks; ++t) {
+    const int cur = t & 1;
+    const float *mine = tr_at(cur, s, cl);
+    float recurrent = 0.f;
+#pragma unroll 16
+    for (int j = 0; j < 64; ++j) recurrent = __fadd_rn(recurrent, __fmul_rn(wr[j], mine[j]));
+    float neighbor = 0.f;
+    if (exc) {
+      if (col > 0) {
+        const float *left = cl > 0 ? tr_at(cur, s, cl - 1) : cluster.map_shared_rank(tr_at(cur, s, CPC - 1), g - 1);
+        neighbor = neighbor + left[id];
+      }
+      if (col + 1 < a.c) {
+        const float *right = cl + 1 < CPC ? tr_at(cur, s, cl + 1) : cluster.map_shared_rank(tr_at(cur, s, 0), g + 1);
+        neighbor = neighbor + right[id];
+      }
+    }
+    const float voltage = decay * V + (1 - decay) * (current + recurrent + .08f * neighbor);
+    const float spike = (voltage - (exc ? 1.f : .6f) - adapt >= 0 ? 1.f : 0.f) * (1 - last);
+    V = voltage * (1 - spike);
+    trace = .8f * trace + .2f * spike;
+    adapt = .98f * adapt + (exc ? .03f : 0.f) * spike;
+    last = spike;
+    cnt = cnt + spike;
+    tr_at(cur ^ 1, s, cl)[id] = trace;
+    const unsigned fired = __ballot_sync(0xffffffffu, live && spike != 0.f);
+    if ((tid & 31) == 0 && fired) atomicAdd(a.spikes + (long)b * a.spikes_ld, __popc(fired));
+    cluster.sync(); // new traces visible cluster-wide; old buffer free for reuse
+  }
+  if (!live) return;
+  st[i] = V;
+  st[n + i] = trace;
+  st[2 * n + i] = adapt;
+  st[3 * n + i] = last;
+  st[4 * n + a.w + i] = cnt;
+  const int oi = a.tab.out_idx[id];
+  if (a.feat && oi >= 0) {
+    const int no = a.tab.n_out;
+    float *f = a.feat + (long)b * (2 * a.c * no);
+    f[col * no + oi] = V;
+    f[a.c * no + col * no + oi] = trace;
+  }
+}
+
+template <int CPC, int SB> size_t ticks_cluster_smem() {
+  return sizeof(float) * (CPC * 64 * TK_LD + 2 * SB * CPC * 64);
+}
+
+template <int CPC, int SB> void configure_ticks_cluster() {
+  cudaFuncSetAttribute(k_ticks_cluster<CPC, SB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)ticks_cluster_smem<CPC, SB>());
+}
+
+template <int CPC, int SB> cudaError_t run_ticks_cluster(const TickArgs &a, int ticks, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.c / CPC, (a.B + SB - 1) / SB, 1);
+  cfg.blockDim = dim3(64 * CPC * SB, 1, 1);
+  cfg.dynamicSmemBytes = ticks_cluster_smem<CPC, SB>();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.c / CPC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_ticks_cluster<CPC, SB>, a, ticks);
+}
+
 __global__ void k_copy_rows(const float *src, long src_ld, float *dst, long dst_ld, int n, int B) {
   const int b = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
@@ -373,6 +537,11 @@ __global__ void k_activity(const int *counts, int A, int R, int n, int T, float 
 } // namespace
 
 void configure_lang_kernels() {
+  configure_ticks_cluster<4, 1>();
+  configure_ticks_cluster<4, 2>();
+  configure_ticks_cluster<4, 4>();
+  configure_ticks_cluster<2, 4>();
+  configure_ticks_cluster<1, 4>();
   configure_gemm<8, 1>();
   configure_gemm<16, 2>();
   configure_gemm<32, 4>();
@@ -389,6 +558,11 @@ void preload_lang_kernels() {
                            (const void *)k_gemm<32, 4>,
                            (const void *)k_gemm<64, 4>,
                            (const void *)k_tick,
+                           (const void *)k_ticks_cluster<4, 1>,
+                           (const void *)k_ticks_cluster<4, 2>,
+                           (const void *)k_ticks_cluster<4, 4>,
+                           (const void *)k_ticks_cluster<2, 4>,
+                           (const void *)k_ticks_cluster<1, 4>,
                            (const void *)k_copy_rows,
                            (const void *)k_norm,
                            (const void *)k_activity};
@@ -436,6 +610,24 @@ void launch_projection(const ProjArgs &a, cudaStream_t s) {
   pb.a[0] = a;
   pb.count = 1;
   launch_projections(pb, s);
+}
+
+bool launch_ticks_cluster(const TickArgs &a, int ticks, cudaStream_t s) {
+  // Columns per CTA so that the cluster (c / CPC CTAs) is at most 8 wide.
+  cudaError_t e;
+  if (a.c % 4 == 0 && a.c / 4 <= 8) {
+    if (a.B == 1) e = run_ticks_cluster<4, 1>(a, ticks, s);
+    else if (a.B == 2) e = run_ticks_cluster<4, 2>(a, ticks, s);
+    else e = run_ticks_cluster<4, 4>(a, ticks, s);
+  } else if (a.c % 2 == 0 && a.c / 2 <= 8) {
+    e = run_ticks_cluster<2, 4>(a, ticks, s);
+  } else if (a.c <= 8) {
+    e = run_ticks_cluster<1, 4>(a, ticks, s);
+  } else {
+    return false;
+  }
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cluster tick launch: ") + cudaGetErrorString(e));
+  return true;
 }
 
 void launch_tick(const TickArgs &a, cudaStream_t s) {

@@ -68,6 +68,10 @@ struct TickArgs {
   UnitTables tab;
 };
 void launch_tick(const TickArgs &a, cudaStream_t s);
+// All `ticks` ticks of one region in one thread-block-cluster launch (trace
+// read from and written back to the state; tr_in/tr_out unused).  Returns
+// false, launching nothing, when the column count has no cluster shape.
+bool launch_ticks_cluster(const TickArgs &a, int ticks, cudaStream_t s);
 
 // Copy trace src (stride src_ld) -> dst (stride dst_ld), n floats per session.
 void launch_copy_rows(const float *src, long src_ld, float *dst, long dst_ld,

@@ -253,3 +253,29 @@ print('ok')
     env = dict(os.environ, NEUROGEN_PROJ_TILE=tile)
     out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0 and 'ok' in out.stdout, out.stderr[-2000:]
+
+
+@pytest.mark.parametrize('columns,ticks,batch', [
+    (3, 3, 1),    # cluster of 3 CTAs, one column each
+    (8, 2, 2),    # cluster of 2 CTAs, four columns each, two sessions per CTA
+    (6, 3, 5),    # cluster of 3, two columns each, ragged session tile
+    (9, 3, 3),    # no cluster shape: one launch per tick
+    (1, 1, 1),    # single column, single tick
+])
+def test_tick_paths_match_reference(columns, ticks, batch):
+    """Every tick-kernel shape (cluster widths, columns per CTA, the per-tick fallback) against
+    the reference library, several sessions at once."""
+    cfg = LanguageConfig(columns=columns, width=24, regions=2, ticks=ticks, idle_steps=1)
+    w = init_packed_weights(cfg, seed=columns * 10 + ticks)
+    rng = np.random.default_rng(columns)
+    w = (w + rng.normal(0, 0.2, w.size)).astype(np.float32)  # non-uniform recurrent weights
+    eng, ref = NativeEngine(cfg, w), RefEngine(cfg, w)
+    sb = np.zeros((batch, ref.S), np.float32)
+    sr = [np.zeros(ref.S, np.float32) for _ in range(batch)]
+    for t in range(8):
+        toks = rng.integers(0, 264, batch)
+        lb, sb, ab, hb = eng.step_batch(toks, sb)
+        for b in range(batch):
+            lr, sr[b], ar, hr = ref.step(int(toks[b]), sr[b])
+            np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+            assert_state_close(cfg, sb[b], sr[b])
