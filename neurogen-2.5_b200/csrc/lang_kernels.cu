@@ -160,8 +160,11 @@ __device__ __forceinline__ void load_x(const float *p, float (&x)[TN]) {
   for (int s = 0; s < TN; ++s) x[s] = f[s];
 }
 
-// Packed pairs of fp32 (sm_100 f32x2): each lane of a .f32x2 op is one IEEE
-// round-to-nearest fp32 op, so pairing two independent chains changes no bit.
+// Packed pairs of fp32 (sm_100 f32x2): each lane of add.rn.f32x2 is one IEEE
+// round-to-nearest fp32 add, so pairing two independent chains changes no
+// bit.  Products stay scalar __fmul_rn: a packed multiply feeding a packed add
+// is contracted into a fused multiply-add by the assembler (measured on
+// B200), which would change the rounding.
 typedef unsigned long long f32x2;
 __device__ __forceinline__ f32x2 pack2(float lo, float hi) {
   f32x2 r;
@@ -170,11 +173,6 @@ __device__ __forceinline__ f32x2 pack2(float lo, float hi) {
 }
 __device__ __forceinline__ void unpack2(f32x2 v, float &lo, float &hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
-  f32x2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
 }
 __device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
   f32x2 r;
@@ -231,15 +229,13 @@ __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
     const int kc = min(GM_KC, a.K - ch * GM_KC);
     auto step = [&](int k) {
       const float4 wv = *reinterpret_cast<const float4 *>(ws + k * 32 + tx * 4);
-      const f32x2 w01 = pack2(wv.x, wv.y), w23 = pack2(wv.z, wv.w);
       float xr[TN];
       load_x<TN>(xs + k * BN + ty * TN, xr);
       f32x2 pr[2][TN];
 #pragma unroll
       for (int s = 0; s < TN; ++s) {
-        const f32x2 xx = pack2(xr[s], xr[s]);
-        pr[0][s] = mul2(w01, xx);
-        pr[1][s] = mul2(w23, xx);
+        pr[0][s] = pack2(__fmul_rn(wv.x, xr[s]), __fmul_rn(wv.y, xr[s]));
+        pr[1][s] = pack2(__fmul_rn(wv.z, xr[s]), __fmul_rn(wv.w, xr[s]));
       }
 #pragma unroll
       for (int s = 0; s < TN; ++s) {
