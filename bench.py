@@ -8,6 +8,9 @@ Workloads (seeded synthetic inputs of the benchmark configurations):
   bsr262k   the same with the 16x16 block matrix (128 block-columns per block-row, 25% fill).
   tick8k    isolated tick: N=8,192 Erdos-Renyi 2%, lognormal fp32 weights, Bernoulli(0.02)
             conductance drive; one step = 1,000 ticks.  metric ticks/s.
+  partitioned4m  N=4,194,304, fan-in 1,000, fp16, imposed Bernoulli(0.01); under torchrun the
+            neurons are row-partitioned over the ranks with a per-tick NCCL all-gather of the
+            spike bitmask (one network: strong scaling); one step = 1,000 ticks.
   bc250     BC-250 language core, seed-0 weights, batch 1, one step = 512 tokens.  tokens/s.
   sessions  BC-250, 256 independent sessions (split over the ranks), one step = 64 tokens per
             session.  tokens/s.
@@ -45,7 +48,7 @@ def parse():
     p.add_argument('--steps', type=int, default=5)
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--workload', default='tick262k',
-                   choices=['tick262k', 'bsr262k', 'tick8k', 'bc250', 'sessions'])
+                   choices=['tick262k', 'bsr262k', 'tick8k', 'partitioned4m', 'bc250', 'sessions'])
     p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     p.add_argument('--rate', type=float, default=0.03)
     p.add_argument('--no-cpu-baseline', action='store_true')
@@ -89,6 +92,14 @@ class Dist:
         import torch
         t = torch.tensor([x], dtype=torch.float64, device='cuda')
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device='cuda')
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -157,8 +168,10 @@ def cuda_timer(fn, stream):
 # ---------------------------------------------------------------------------
 # Tick-network workloads.
 # ---------------------------------------------------------------------------
-def tick_config(name, rate):
-    from neurogen_b200.network import scaled_262k, isolated_8k
+def tick_config(name, rate, rank=0, world=1):
+    from neurogen_b200.network import scaled_262k, isolated_8k, partitioned_4m
+    if name == 'partitioned4m':
+        return partitioned_4m(rank, world, rate=0.01), 1000, 'partitioned_4194304_fanin1000'
     if name == 'tick262k':
         return scaled_262k('csr', rate=rate), 10000, 'scaled_tick_262144_csr'
     if name == 'bsr262k':
@@ -166,7 +179,7 @@ def tick_config(name, rate):
     return isolated_8k(), 1000, 'isolated_tick_8192'
 
 
-def tick_bytes(cfg, spikes, events):
+def tick_bytes(cfg, spikes, events, held=None):
     """Algorithmic DRAM bytes of one tick (roofline section).
 
     Per neuron: V, adaptation, g_E, g_I (fp32) and refractory (int32) read and written (40 B),
@@ -174,27 +187,37 @@ def tick_bytes(cfg, spikes, events):
     synapse count (20 B).  Per delivered synapse: the packed post/delay word and the weight.
     """
     wbytes = 2 if cfg.weight_kind == 1 else 4
+    held = cfg.n if held is None else held
     if cfg.storage == 1:
         # Block storage: per spiking neuron and block of its block-column, one 32-byte tile
         # column plus the block's 4-byte row/delay word; events counted per non-zero.
         blocks_per_col = cfg.bsr_blocks
-        return cfg.n * 56 + spikes * (16 + blocks_per_col * 36)
-    return cfg.n * 56 + spikes * 20 + events * (4 + wbytes)
+        return held * 56 + spikes * (16 + blocks_per_col * 36)
+    return held * 56 + spikes * 20 + events * (4 + wbytes)
 
 
 def bench_ticks(args, dist):
     import torch
     from neurogen_b200 import library
-    from neurogen_b200.network import Topology
+    from neurogen_b200.network import Topology, Network, nccl_unique_id
     lib = library()
-    cfg, ticks, wl = tick_config(args.workload, args.rate)
+    part = args.workload == 'partitioned4m'
+    cfg, ticks, wl = tick_config(args.workload, args.rate, dist.rank, dist.world)
     ticks = args.ticks or ticks
-    cfg.seed = cfg.seed + dist.rank  # independent replica per rank
+    if not part:
+        cfg.seed = cfg.seed + dist.rank  # independent replica per rank
     t0 = time.time()
-    topo = Topology(cfg)
-    net = topo.network()
+    if part and dist.world > 1:
+        ids = [nccl_unique_id() if dist.rank == 0 else None]
+        dist.pg.broadcast_object_list(ids, src=0)
+        net = Network.partitioned(cfg, ids[0])
+        synapses = net.synapses * dist.world
+    else:
+        topo = Topology(cfg)
+        net = topo.network()
+        synapses = topo.synapses
     setup_s = time.time() - t0
-    split = cfg.launch == 2 or (cfg.launch == 0 and cfg.n >= 65536)
+    split = part or cfg.launch == 2 or (cfg.launch == 0 and cfg.n >= 65536)
     stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
@@ -216,11 +239,16 @@ def bench_ticks(args, dist):
     t_max = dist.max(elapsed)
     total_ticks = ticks * args.steps
     per_tick_s = elapsed / total_ticks
-    b_tick = tick_bytes(cfg, spikes / total_ticks, events / total_ticks)
+    held = cfg.n // dist.world if part else cfg.n
+    b_tick = tick_bytes(cfg, spikes / total_ticks, events / total_ticks, held)
     pk, src = peaks()
-    achieved = b_tick / per_tick_s / 1e9
+    if part:  # one network over all ranks: sum the ranks' bytes, compare with all their peaks
+        b_tick = dist.sum(b_tick)
+        spikes, events = dist.sum(spikes), dist.sum(events)
+    achieved = b_tick / (t_max / total_ticks) / 1e9
+    peak_total = pk['hbm_gbs'] * (dist.world if part else 1)
     line = {
-        'metric': METRIC_TICKS, 'value': total_ticks * dist.world / t_max, 'unit': 'ticks/s',
+        'metric': METRIC_TICKS, 'value': total_ticks * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
         'n_gpus': dist.world, 'steps': args.steps, 'warmup': args.warmup,
         'ms_per_step': t_max / args.steps * 1e3, 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic',
@@ -228,24 +256,27 @@ def bench_ticks(args, dist):
                    'fanin': cfg.fanin if cfg.topology == 1 else None,
                    'bsr': [cfg.bsr_blocks, cfg.bsr_fill] if cfg.topology == 2 else None,
                    'spike_rate': spikes / total_ticks / cfg.n, 'weights': 'fp16' if cfg.weight_kind else 'fp32',
-                   'delays': [cfg.delay_min, cfg.delay_max], 'synapses': topo.synapses,
-                   'l2': 'inputs larger than L2' if topo.synapses * 6 > 126e6 else 'network fits in L2',
-                   'parallelism': f'replicas{dist.world}', 'setup_s': round(setup_s, 2)},
-        'synaptic_events_per_s': events * dist.world / t_max,
-        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
-                     'frac': achieved / pk['hbm_gbs'], 'traffic': None,
-                     'bytes_per_launch': b_tick, 'kernel': 'k_net_tick', 'peak_source': src},
+                   'delays': [cfg.delay_min, cfg.delay_max], 'synapses': synapses,
+                   'l2': 'inputs larger than L2' if synapses * 6 > 126e6 else 'network fits in L2',
+                   'parallelism': (f'rows{dist.world} + NCCL bitmask all-gather' if part and dist.world > 1
+                                   else f'replicas{dist.world}'),
+                   'setup_s': round(setup_s, 2)},
+        'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
+        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
+                     'frac': achieved / peak_total, 'traffic': None, 'bytes_per_tick': b_tick,
+                     'kernel': 'tick = k_net_alif + k_net_push' if split else 'k_net_fused',
+                     'peak_source': src},
         'gpu_launches': total_ticks * (2 if split else 1) + args.steps * (-(-ticks // 64) + 1),
         'clocks': clk.summary(),
     }
     if not args.no_e2e:
-        line['e2e'] = e2e_ticks(args, lib, net, cfg, ticks, dist)
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line['e2e'] = e2e_ticks(args, lib, net, cfg, ticks, dist, part)
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and not part:
         line['cpu_baseline'] = cpu_baseline_ticks(cfg, topo)
     return line
 
 
-def e2e_ticks(args, lib, net, cfg, ticks, dist):
+def e2e_ticks(args, lib, net, cfg, ticks, dist, part=False):
     """Through the C ABI with host buffers: per step, upload the full network state from
     pinned host memory, run the ticks, read back the spike/event totals and the state."""
     import ctypes as ct
@@ -276,7 +307,7 @@ def e2e_ticks(args, lib, net, cfg, ticks, dist):
     dist.barrier()
     elapsed = sum(step() for _ in range(args.steps))
     t_max = dist.max(elapsed)
-    return {'value': ticks * args.steps * dist.world / t_max, 'unit': 'ticks/s',
+    return {'value': ticks * args.steps * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
             'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
             'api': 'ng_net_set_state + ng_net_run + ng_net_stats + ng_net_get_state (host buffers)'}
 
@@ -439,10 +470,18 @@ def cpu_baseline_lang(cfg, w, toks, budget_s=10.0):
 def reference_arm(args):
     import multiprocessing
     cores = multiprocessing.cpu_count()
-    if args.workload in ('tick262k', 'bsr262k', 'tick8k'):
+    if args.workload in ('tick262k', 'bsr262k', 'tick8k', 'partitioned4m'):
         from neurogen_b200.network import Topology
         from oracle.net import NetOracle
         cfg, ticks, wl = tick_config(args.workload, args.rate)
+        scale = 1
+        if args.workload == 'partitioned4m':
+            # 4.2 billion synapses do not fit a host-side checker: run 1/16 of the neurons with
+            # the same fan-in and rate, and scale the time per tick by 16 (work per tick is
+            # proportional to the neuron count).
+            scale = 16
+            cfg.n //= scale
+            cfg.n_exc //= scale
         orc = NetOracle(cfg, *Topology(cfg).export())
         sample = 20 if cfg.n > 100000 else 200
         for _ in range(args.warmup):
@@ -451,8 +490,10 @@ def reference_arm(args):
         for _ in range(args.steps):
             orc.run_mt(sample)
         el = time.time() - t0
-        value, unit = sample * args.steps / el, 'ticks/s'
+        value, unit = sample * args.steps / el / scale, 'ticks/s'
         kind, desc = 'port', f'{sample} ticks per step of {wl} (oracle/net_oracle.c, OpenMP)'
+        if scale > 1:
+            desc += f'; 1/{scale}-scale network (N={cfg.n:,}), time per tick x{scale}'
         metric = METRIC_TICKS
     else:
         from neurogen_b200.language import LanguageConfig, init_packed_weights

@@ -164,7 +164,9 @@ typedef struct {
   int32_t storage;              /* 0 = CSR push, 1 = BSR push (BSR16 topology) */
   int32_t launch;               /* 0 = auto, 1 = one fused launch per tick,
                                    2 = split membrane / push launches            */
-  int32_t reserved[6];
+  int32_t part_rank, part_world; /* neuron row-partition: this rank owns neurons
+                                   [rank*n/world, (rank+1)*n/world); 0/1 = whole */
+  int32_t reserved[4];
 } ng_net_config;
 
 /* Fill `cfg` with the biology.py defaults (BiologyConfig, biology.py:19-77;
@@ -183,6 +185,18 @@ void *ng_net_create_edges(const ng_net_config *cfg, int64_t n_syn,
                           const int32_t *delay, const float *weight);
 void ng_net_destroy(void *net);
 
+/* Neuron-partitioned network over `part_world` GPUs (one process per GPU):
+ * this rank owns the neurons [rank*n/world, (rank+1)*n/world) -- their state,
+ * their delay-ring slots and every synapse that ends on them -- and the ranks
+ * all-gather the per-tick spike bitmask (n/8 bytes in total) with NCCL over
+ * NVLink.  Every rank calls this collectively with the same cfg (part_rank set
+ * to its own rank) and the same 128-byte NCCL unique id from
+ * ng_nccl_unique_id on one rank.  n must be a multiple of 32 * world; CSR
+ * storage only.  Spikes and state equal those of the unpartitioned network. */
+void *ng_net_create_partitioned(const ng_net_config *cfg, const void *nccl_id);
+/* Fills `id` (128 bytes) with a fresh NCCL unique id. */
+int ng_nccl_unique_id(void *id);
+
 /* Host-only topology: generate the synapses of `cfg` without a GPU (the same
  * synapses ng_net_create would build), export them, or build a device network
  * from them.  Lets a CPU checker and the GPU share one generated network. */
@@ -194,13 +208,15 @@ int ng_topology_export(const void *topology, int32_t *pre, int32_t *post,
 void *ng_net_create_topology(const void *topology);
 
 /* Synapse count, and export of the (generated) synapse list in the order
- * pre-major (arrays sized ng_net_synapses). */
+ * pre-major (arrays sized ng_net_synapses).  For a partitioned network: this
+ * rank's synapses, with global neuron indices. */
 int64_t ng_net_synapses(void *net);
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay,
                   float *weight);
 
 /* State: v, adapt, g_exc, g_inh (fp32 [n] each), refractory ticks (int32 [n]),
- * delay ring (int32 [16][n][2]) and the tick counter.  NULL pointers skip. */
+ * delay ring (int32 [16][n][2]) and the tick counter.  NULL pointers skip.
+ * For a partitioned network n is this rank's neuron count. */
 int ng_net_set_state(void *net, const float *v, const float *adapt,
                      const float *g_exc, const float *g_inh,
                      const int32_t *refractory, const int32_t *ring,
@@ -210,7 +226,8 @@ int ng_net_get_state(void *net, float *v, float *adapt, float *g_exc,
                      int64_t *tick);
 
 /* Advance `ticks` ticks.  spikes (host, may be NULL): [ticks][ceil(n/32)]
- * uint32 bitmask words, bit (i % 32) of word i/32 = neuron i spiked.
+ * uint32 bitmask words, bit (i % 32) of word i/32 = neuron i spiked (for a
+ * partitioned network: the whole network's bitmask, on every rank).
  * counts (host, may be NULL): [ticks] spikes per tick. */
 int ng_net_run(void *net, int ticks, uint32_t *spikes, int64_t *counts);
 

@@ -1,6 +1,7 @@
 // C ABI of the isolated-tick spiking network (include/neurogen_b200.h part 4).
 #include "capi_common.h"
 #include "net_engine.h"
+#include "nccl_dl.h"
 #include "neurogen_b200.h"
 
 #include <cstring>
@@ -47,11 +48,14 @@ void ng_net_default_config(ng_net_config *c) {
   c->drive_ns = 4.f;
   c->storage = 0;
   c->launch = 0;
+  c->part_rank = 0;
+  c->part_world = 0;
 }
 
 void *ng_net_create(const ng_net_config *cfg) {
   return guarded_ptr([&]() -> void * {
     if (!cfg) throw std::invalid_argument("Null network config");
+    if (cfg->part_world > 1) throw std::invalid_argument("Use ng_net_create_partitioned for part_world > 1");
     std::unique_ptr<Topology> t(make_topology(*cfg));
     return new Network(*t);
   });
@@ -70,6 +74,25 @@ void *ng_net_create_topology(const void *topology) {
   return guarded_ptr([&]() -> void * {
     if (!topology) throw std::invalid_argument("Null topology");
     return new Network(*static_cast<const Topology *>(topology));
+  });
+}
+
+void *ng_net_create_partitioned(const ng_net_config *cfg, const void *nccl_id) {
+  return guarded_ptr([&]() -> void * {
+    if (!cfg) throw std::invalid_argument("Null network config");
+    if (cfg->part_world < 2) throw std::invalid_argument("ng_net_create_partitioned needs part_world >= 2");
+    if (!nccl_id) throw std::invalid_argument("Null NCCL unique id");
+    std::unique_ptr<Topology> t(make_topology(*cfg));
+    return new Network(*t, nccl_id);
+  });
+}
+
+int ng_nccl_unique_id(void *id) {
+  return guarded([&] {
+    if (!id) throw std::invalid_argument("Null output");
+    ncclUniqueId u;
+    nccl_check(nccl().GetUniqueId(&u), "ncclGetUniqueId");
+    std::memcpy(id, &u, sizeof u);
   });
 }
 

@@ -7,6 +7,7 @@
 // rounded onto the delay ring's fixed-point grid (multiples of 2^-24 nS):
 // fp16 weights already are; fp32 weights are rounded once at generation.
 #include "net_engine.h"
+#include "nccl_dl.h"
 
 #include <cuda_fp16.h>
 
@@ -134,27 +135,48 @@ void validate_config(const ng_net_config &c) {
   }
   if (c.storage == 1 && c.topology != NG_TOPO_BSR16)
     throw std::invalid_argument("Block storage needs the 16x16 block topology");
+  if (c.part_world < 0 || c.part_world > 1024) throw std::invalid_argument("part_world must be in 0..1024");
+  if (c.part_world > 1) {
+    if (c.part_rank < 0 || c.part_rank >= c.part_world) throw std::invalid_argument("part_rank must be in 0..part_world-1");
+    if (c.n % (32 * c.part_world)) throw std::invalid_argument("A partitioned network needs n divisible by 32 * part_world");
+    if (c.storage != 0 || c.topology == NG_TOPO_BSR16)
+      throw std::invalid_argument("A partitioned network uses CSR storage with Erdos-Renyi or fixed fan-in topology");
+  }
 }
 
 // ---------------------------------------------------------------------------
 // CSR generation.
 // ---------------------------------------------------------------------------
+// Postsynaptic range [lo, hi) held by this partition (the whole network when
+// unpartitioned).
+static void partition_range(const ng_net_config &c, int &lo, int &hi) {
+  const int world = c.part_world > 1 ? c.part_world : 1;
+  const int rank = c.part_world > 1 ? c.part_rank : 0;
+  lo = int((long long)c.n * rank / world);
+  hi = int((long long)c.n * (rank + 1) / world);
+}
+
 void generate_csr(const ng_net_config &c, HostCSR &out) {
   const int n = c.n;
+  int lo = 0, hi = n;
+  partition_range(c, lo, hi);
+  const int np = hi - lo;
   out.n = n;
+  out.post_base = lo;
+  out.n_post = np;
   const WeightDraw wd(c);
   const Stream edge(c.seed, S_EDGE), pres(c.seed, S_PRE), dly(c.seed, S_DELAY);
   const uint64_t dspan = uint64_t(c.delay_max - c.delay_min + 1);
   const bool half = c.weight_kind == NG_W_HALFNORMAL_F16;
-  std::vector<double> sum_e(n, 0.0), sum_i(n, 0.0);
+  std::vector<double> sum_e(np, 0.0), sum_i(np, 0.0);
 
   if (c.topology == NG_TOPO_ERDOS_RENYI) {
-    // Row by row (presynaptic), posts in ascending order.
+    // Row by row (presynaptic), held posts in ascending order.
     std::vector<long long> count(n, 0);
 #pragma omp parallel for schedule(dynamic, 64)
     for (int i = 0; i < n; ++i) {
       long long k = 0;
-      for (int j = 0; j < n; ++j)
+      for (int j = lo; j < hi; ++j)
         if (j != i && edge.uniform(uint64_t(i), uint64_t(j)) < double(c.p_connect)) ++k;
       count[i] = k;
     }
@@ -165,10 +187,10 @@ void generate_csr(const ng_net_config &c, HostCSR &out) {
     for (int i = 0; i < n; ++i) {
       long long e = out.row[i];
       const bool inh = i >= c.n_exc;
-      for (int j = 0; j < n; ++j) {
+      for (int j = lo; j < hi; ++j) {
         if (j == i || !(edge.uniform(uint64_t(i), uint64_t(j)) < double(c.p_connect))) continue;
         const int d = c.delay_min + int(dly.below(uint64_t(i), uint64_t(j), dspan));
-        out.syn[e] = pack_word(j, d);
+        out.syn[e] = pack_word(j - lo, d);
         uint16_t hb = 0;
         const float w = wd.draw(uint64_t(i), uint64_t(j), inh, &hb);
         if (half) out.w16[e] = hb;
@@ -183,40 +205,56 @@ void generate_csr(const ng_net_config &c, HostCSR &out) {
         (w < 0 ? sum_i : sum_e)[out.syn[e] & kPostMask] += std::fabs(w);
       }
   } else if (c.topology == NG_TOPO_FIXED_FANIN) {
-    // Each post draws `fanin` uniform presynaptic cells (no autapse: a draw of
-    // the post itself moves to the next cell), then a stable scatter by pre.
+    // Each held post j draws `fanin` uniform presynaptic cells keyed (j, k) (no
+    // autapse: a draw of j itself moves to the next cell).  Two passes over a
+    // fixed split of the posts into kChunks: count per (chunk, pre), then each
+    // chunk writes its synapses in post order at its own offsets -- rows come
+    // out in ascending post order whatever the thread count, without holding
+    // every synapse twice.
     const int K = c.fanin;
-    const size_t total = size_t(n) * K;
-    std::vector<int> tpre(total);
-    std::vector<uint32_t> tword(total);
-    std::vector<float> tw32(half ? 0 : total);
-    std::vector<uint16_t> tw16(half ? total : 0);
-#pragma omp parallel for schedule(static)
-    for (int j = 0; j < n; ++j)
-      for (int k = 0; k < K; ++k) {
-        int pre = int(pres.below(uint64_t(j), uint64_t(k), uint64_t(n)));
-        if (pre == j) pre = (pre + 1) % n;
-        const size_t x = size_t(j) * K + k;
-        tpre[x] = pre;
-        tword[x] = pack_word(j, c.delay_min + int(dly.below(uint64_t(j), uint64_t(k), dspan)));
-        uint16_t hb = 0;
-        const float w = wd.draw(uint64_t(j), uint64_t(k), pre >= c.n_exc, &hb);
-        if (half) tw16[x] = hb;
-        else tw32[x] = w;
-      }
+    constexpr int kChunks = 8;
+    auto chunk_lo = [&](int ch) { return lo + int((long long)np * ch / kChunks); };
+    auto draw_pre = [&](int j, int k) {
+      int pre = int(pres.below(uint64_t(j), uint64_t(k), uint64_t(n)));
+      return pre == j ? (pre + 1) % n : pre;
+    };
+    std::vector<int> cnt(size_t(kChunks) * n, 0);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int ch = 0; ch < kChunks; ++ch) {
+      int *cc = cnt.data() + size_t(ch) * n;
+      for (int j = chunk_lo(ch); j < chunk_lo(ch + 1); ++j)
+        for (int k = 0; k < K; ++k) ++cc[draw_pre(j, k)];
+    }
     std::vector<long long> count(n, 0);
-    for (size_t x = 0; x < total; ++x) ++count[tpre[x]];
+    for (int ch = 0; ch < kChunks; ++ch)
+      for (int i = 0; i < n; ++i) count[i] += cnt[size_t(ch) * n + i];
     finish_rows(out, count);
     if (half) out.w16.assign(out.syn.size(), 0);
     else out.w32.assign(out.syn.size(), 0.f);
-    std::vector<long long> fill(out.row.begin(), out.row.end() - 1);
-    for (size_t x = 0; x < total; ++x) {
-      const long long e = fill[tpre[x]]++;
-      out.syn[e] = tword[x];
-      if (half) out.w16[e] = tw16[x];
-      else out.w32[e] = tw32[x];
-      const double w = half ? double(__half2float(__ushort_as_half(tw16[x]))) : double(tw32[x]);
-      (w < 0 ? sum_i : sum_e)[x / K] += std::fabs(w);
+    // cursor[ch][pre]: where chunk ch writes its first synapse of row pre.
+    std::vector<long long> cursor(size_t(kChunks) * n);
+    for (int i = 0; i < n; ++i) {
+      long long at = out.row[i];
+      for (int ch = 0; ch < kChunks; ++ch) {
+        cursor[size_t(ch) * n + i] = at;
+        at += cnt[size_t(ch) * n + i];
+      }
+    }
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int ch = 0; ch < kChunks; ++ch) {
+      long long *cur = cursor.data() + size_t(ch) * n;
+      for (int j = chunk_lo(ch); j < chunk_lo(ch + 1); ++j)
+        for (int k = 0; k < K; ++k) {
+          const int pre = draw_pre(j, k);
+          const long long e = cur[pre]++;
+          out.syn[e] = pack_word(j - lo, c.delay_min + int(dly.below(uint64_t(j), uint64_t(k), dspan)));
+          uint16_t hb = 0;
+          const float w = wd.draw(uint64_t(j), uint64_t(k), pre >= c.n_exc, &hb);
+          if (half) out.w16[e] = hb;
+          else out.w32[e] = w;
+          const double wa = half ? double(__half2float(__ushort_as_half(hb))) : double(w);
+          (wa < 0 ? sum_i : sum_e)[j - lo] += std::fabs(wa); // post j belongs to this chunk only
+        }
     }
     for (int i = 0; i < n; ++i) out.outdeg[i] = int(count[i]);
   } else {
@@ -247,7 +285,7 @@ void generate_csr(const ng_net_config &c, HostCSR &out) {
         out.outdeg[pre] = int(count[pre]);
       }
   }
-  check_ring_bound(n, sum_e, sum_i);
+  check_ring_bound(np, sum_e, sum_i);
 }
 
 // ---------------------------------------------------------------------------
@@ -331,6 +369,8 @@ void csr_from_edges(const ng_net_config &c, int64_t nnz, const int32_t *pre, con
                     const int32_t *delay, const float *w, HostCSR &out) {
   const int n = c.n;
   out.n = n;
+  out.post_base = 0;
+  out.n_post = n;
   if (nnz < 0 || (nnz > 0 && (!pre || !post || !delay || !w)))
     throw std::invalid_argument("Null synapse arrays");
   std::vector<long long> count(n, 0);
@@ -394,7 +434,7 @@ void Topology::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *
   for (int i = 0; i < csr.n; ++i)
     for (long long e = csr.row[i]; e < csr.row[i + 1]; ++e) {
       const float w = half ? __half2float(__ushort_as_half(csr.w16[e])) : csr.w32[e];
-      if (w != 0.f) emit(i, int(csr.syn[e] & kPostMask), int(csr.syn[e] >> 28) + 1, w);
+      if (w != 0.f) emit(i, csr.post_base + int(csr.syn[e] & kPostMask), int(csr.syn[e] >> 28) + 1, w);
     }
 }
 
@@ -441,15 +481,22 @@ template <class T> DeviceBuffer upload_padded(const std::vector<T> &v, size_t pa
 float decay_of(float dt, float tau) { return float(std::exp(-double(dt) / double(tau))); }
 } // namespace
 
-Network::Network(const Topology &topo) : cfg(topo.cfg) {
+Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
   const ng_net_config &c = topo.cfg;
   const HostCSR *csr = topo.blocks ? nullptr : &topo.csr;
   const HostBSR *bsr = topo.blocks ? &topo.bsr : nullptr;
   device = require_sm100_device();
-  n_ = c.n;
+  // Held neurons [base, base + n_) of a network of n_pre_ neurons.
+  n_pre_ = c.n;
+  n_ = csr ? csr->n_post : c.n;
+  base_ = csr ? csr->post_base : 0;
+  world_ = c.part_world > 1 ? c.part_world : 1;
+  rank_ = world_ > 1 ? c.part_rank : 0;
   NetDev &d = dev_;
   d.n = n_;
   d.n_exc = c.n_exc;
+  d.n_pre = n_pre_;
+  d.base = base_;
   if (bsr) {
     bcol_ = upload_vec(bsr->bcol);
     blk_ = upload_vec(bsr->blk);
@@ -516,28 +563,48 @@ Network::Network(const Topology &topo) : cfg(topo.cfg) {
   d.drive_thr = thr >= 4294967295.0 ? 0xFFFFFFFFu : uint32_t(thr);
   d.drive_key = mix64(c.seed ^ 0xD41Eull);
   d.ref_ticks = int(std::lround(double(c.t_ref_ms) / double(c.dt_ms)));
-  // Current bitmask (padded to whole 256-neuron groups), per-group totals, tick.
-  const size_t groups = (N + kNetBlock - 1) / kNetBlock;
-  bitmask_.reset(groups * (kNetBlock / 32) * 4);
+  // Whole-network bitmask (padded to whole 256-neuron groups), per-group
+  // totals (enough pairs for the held groups and the presynaptic groups), tick.
+  const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
+  const size_t groups = std::max(pre_groups, (N + kNetBlock - 1) / kNetBlock);
+  bitmask_.reset(pre_groups * (kNetBlock / 32) * 4);
   totals_.reset(groups * 2 * sizeof(unsigned long long));
   tick_dev_.reset(sizeof(long long));
-  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, groups * (kNetBlock / 32) * 4));
+  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, pre_groups * (kNetBlock / 32) * 4));
   NGB_CUDA(cudaMemset(totals_.as<void>(), 0, groups * 2 * sizeof(unsigned long long)));
+  totals_pairs_ = groups;
   NGB_CUDA(cudaMemset(tick_dev_.as<void>(), 0, sizeof(long long)));
   d.bitmask = bitmask_.as<uint32_t>();
   d.totals = totals_.as<unsigned long long>();
-  // Small networks: one fused launch per tick; large: split membrane / push.
-  split_ = c.launch == 2 || (c.launch == 0 && n_ >= 65536);
+  // Small networks: one fused launch per tick; large or partitioned: split
+  // membrane / push, with the bitmask all-gather between them.
+  split_ = world_ > 1 || c.launch == 2 || (c.launch == 0 && n_ >= 65536);
+  if (world_ > 1) {
+    if (!nccl_id) throw std::invalid_argument("A partitioned network needs an NCCL unique id");
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    nccl_check(nccl().CommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
+  }
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
 }
 
 Network::~Network() {
-  if (graph_) cudaGraphExecDestroy(graph_);
+  if (graph_) cudaGraphExecDestroy(graph_); // before the communicator its NCCL nodes use
+  if (comm_) nccl().CommDestroy(comm_);
   if (stream) cudaStreamDestroy(stream);
 }
 
 void Network::launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st) {
-  if (split_) {
+  if (world_ > 1) {
+    // Held slice of the bitmask -> every rank's copy of the whole bitmask.
+    const size_t words = size_t(n_) / 32;
+    launch_net_alif(dev_, t, nullptr, counts_row, st);
+    uint32_t *bm = bitmask_.as<uint32_t>();
+    nccl_check(nccl().AllGather(bm + size_t(base_) / 32, bm, words, ncclUint32, comm_, st), "ncclAllGather");
+    if (spikes_row)
+      NGB_CUDA(cudaMemcpyAsync(spikes_row, bm, size_t(n_pre_) / 32 * 4, cudaMemcpyDeviceToDevice, st));
+    launch_net_push(dev_, t, counts_row, st);
+  } else if (split_) {
     launch_net_alif(dev_, t, spikes_row, counts_row, st);
     launch_net_push(dev_, t, counts_row, st);
   } else {
@@ -566,7 +633,7 @@ void Network::capture_graph() {
 void Network::stats(int64_t *totals) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaDeviceSynchronize());
-  const size_t groups = (size_t(n_) + kNetBlock - 1) / kNetBlock;
+  const size_t groups = totals_pairs_;
   std::vector<unsigned long long> g(groups * 2);
   NGB_CUDA(cudaMemcpy(g.data(), totals_.as<void>(), g.size() * 8, cudaMemcpyDeviceToHost));
   totals[0] = totals[1] = 0;
@@ -594,10 +661,12 @@ void Network::export_edges(int32_t *pre, int32_t *post, int32_t *delay, float *w
     }
   } else {
     HostCSR &h = t.csr;
-    h.n = n_;
-    h.row.resize(size_t(n_) + 1);
+    h.n = n_pre_;
+    h.post_base = base_;
+    h.n_post = n_;
+    h.row.resize(size_t(n_pre_) + 1);
     NGB_CUDA(cudaMemcpy(h.row.data(), row_.as<void>(), h.row.size() * 8, cudaMemcpyDeviceToHost));
-    const size_t total = size_t(h.row[n_]);
+    const size_t total = size_t(h.row[n_pre_]);
     h.syn.resize(total);
     if (total) NGB_CUDA(cudaMemcpy(h.syn.data(), syn_.as<void>(), total * 4, cudaMemcpyDeviceToHost));
     if (dev_.w_half) {
@@ -641,7 +710,7 @@ void Network::get_state(float *v, float *a, float *ge, float *gi, int32_t *ref, 
 
 void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_counts, cudaStream_t st) {
   if (ticks < 0) throw std::invalid_argument("ticks must be non-negative");
-  const size_t words = (size_t(n_) + 31) / 32;
+  const size_t words = (size_t(n_pre_) + 31) / 32;
   if (d_counts) NGB_CUDA(cudaMemsetAsync(d_counts, 0, size_t(ticks) * 16, st));
   int k = 0;
   if (!d_spikes && !d_counts && ticks >= kGraphTicks) {
@@ -658,7 +727,7 @@ void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_count
 
 void Network::run_host(int ticks, uint32_t *spikes, int64_t *counts) {
   NGB_CUDA(cudaSetDevice(device));
-  const size_t words = (size_t(n_) + 31) / 32;
+  const size_t words = (size_t(n_pre_) + 31) / 32;
   const int chunk = 1024;
   if (spikes) rec_spikes_.reset(size_t(std::min(ticks, chunk)) * words * 4 + 4);
   if (counts) rec_counts_.reset(size_t(std::min(ticks, chunk)) * 16 + 16);

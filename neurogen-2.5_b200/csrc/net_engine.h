@@ -3,6 +3,7 @@
 #pragma once
 #include "common.h"
 #include "net_kernels.h"
+#include "nccl_dl.h"
 #include "neurogen_b200.h"
 
 #include <cstdint>
@@ -13,9 +14,10 @@ namespace ngb {
 
 // Synapses by presynaptic neuron, host form.
 struct HostCSR {
-  int n = 0;
+  int n = 0;                     // presynaptic rows (all neurons of the network)
+  int post_base = 0, n_post = 0; // postsynaptic neurons held: [post_base, post_base + n_post)
   std::vector<long long> row;    // [n+1], rows padded to multiples of 8
-  std::vector<uint32_t> syn;     // post | (delay-1) << 28
+  std::vector<uint32_t> syn;     // (post - post_base) | (delay-1) << 28
   std::vector<float> w32;        // signed weights (fp32 storage), or
   std::vector<uint16_t> w16;     // fp16 bits (fp16 storage)
   std::vector<int> outdeg;       // non-zero synapses per row
@@ -53,7 +55,9 @@ void validate_config(const ng_net_config &c);
 
 class Network {
 public:
-  explicit Network(const Topology &topo);
+  // nccl_id: 128-byte NCCL unique id, required when cfg.part_world > 1
+  // (collective: every rank constructs its partition at the same time).
+  explicit Network(const Topology &topo, const void *nccl_id = nullptr);
   ~Network();
   Network(const Network &) = delete;
   Network &operator=(const Network &) = delete;
@@ -76,7 +80,9 @@ public:
   std::mutex mutex;
 
 private:
-  int n_ = 0;
+  int n_ = 0, n_pre_ = 0, base_ = 0, world_ = 1, rank_ = 0;
+  size_t totals_pairs_ = 0;
+  ncclComm_t comm_ = nullptr;
   int64_t nnz_ = 0;
   long long tick_ = 0;
   NetDev dev_{};

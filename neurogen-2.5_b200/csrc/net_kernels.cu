@@ -76,10 +76,11 @@ __device__ __forceinline__ bool alif_update(const NetDev &d, long long t, int i)
   int2 *rp = d.ring + (size_t)slot * d.n + i;
   const int2 r = *rp;
   *rp = make_int2(0, 0);
-  const bool exc = i < d.n_exc;
+  const int gidx = d.base + i; // global neuron index: E/I split and drive draw
+  const bool exc = gidx < d.n_exc;
   float ge = __fadd_rn(__fmul_rn(d.ge[i], d.dE), __fmul_rn(__int2float_rn(r.x), kRingQuantum));
   const float gi = __fadd_rn(__fmul_rn(d.gi[i], d.dI), __fmul_rn(__int2float_rn(r.y), kRingQuantum));
-  const bool ev = drive_event(d, t, i);
+  const bool ev = drive_event(d, t, gidx);
   if (d.drive_kind == 0 && ev) ge = __fadd_rn(ge, d.drive_ns);
   float a = __fmul_rn(d.a[i], d.dA);
   const float g = __fadd_rn(__fadd_rn(d.g_leak, ge), gi);
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
   const int lane = threadIdx.x & 31;
   const bool s = i < d.n ? alif_update(d, t, i) : false;
   const unsigned fired = __ballot_sync(0xffffffffu, s);
-  const int base = i - lane;
+  const int base = i - lane; // fused launches are unpartitioned: base 0
   if (lane == 0 && base < d.n) {
     d.bitmask[base >> 5] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
   if (lane == 0 && base < d.n) {
-    d.bitmask[base >> 5] = fired;
+    d.bitmask[(d.base + base) >> 5] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + 2 * (size_t)blockIdx.x, counts);
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
   const int base = blockIdx.x * TB;
   if (warp == 0) {
     const int w = base / 32 + (lane & 7);
-    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n) ? d.bitmask[w] : 0u;
+    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n_pre) ? d.bitmask[w] : 0u;
     if (BSR) {
       // 16 block-columns per group; lane k < 16 owns half (k & 1) of word k / 2.
       const unsigned wk = __shfl_sync(0xffffffffu, word, (lane >> 1) & 7);
@@ -348,7 +349,7 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
 }
 
 void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, cudaStream_t s) {
-  const int blocks = (d.n + TB - 1) / TB;
+  const int blocks = (d.n_pre + TB - 1) / TB;
   if (d.bsr) k_net_push<true><<<blocks, TB, 0, s>>>(d, t, counts);
   else k_net_push<false><<<blocks, TB, 0, s>>>(d, t, counts);
 }

@@ -14,7 +14,9 @@ constexpr int kTailPad = 16;   // extra zero synapses after the last row
 constexpr uint32_t kPostMask = 0x0FFFFFFFu;
 
 struct NetDev {
-  int n, n_exc;
+  int n, n_exc;  // n: neurons held here (state, ring); n_exc: global E/I split
+  int n_pre;     // presynaptic rows = neurons of the whole network
+  int base;      // global index of the first neuron held here (multiple of 32)
   // CSR by presynaptic neuron, rows padded to multiples of 8 with zero weights.
   const long long *row; // [n+1]
   const uint32_t *syn;  // packed post/delay
@@ -30,9 +32,10 @@ struct NetDev {
   float *v, *a, *ge, *gi;
   int *ref;
   int2 *ring;
-  uint32_t *bitmask;            // this tick's spike words [ceil(n/32)]
-  // Running (spikes, synaptic events) of each membrane CTA's 256 neurons since
-  // creation, [ceil(n/256)][2]; each entry has one writer, so no atomics.
+  uint32_t *bitmask;            // this tick's spike words of the whole network [ceil(n_pre/32)]
+  // Running counters since creation, one pair per 256-neuron group: [g][0]
+  // spikes of held group g (membrane kernel), [g][1] events pushed from
+  // presynaptic group g (push kernel).  One writer per entry, no atomics.
   unsigned long long *totals;
   // Constants (see net_kernels.cu for the exact operation order).
   float dE, dI, dA, g_leak, gLEL, e_inh, v_th, v_reset, cap_e, cap_i, neg_dt, adapt_inc, bias,

@@ -29,6 +29,7 @@ EXPORTS = (
     'ng_net_synapses', 'ng_net_export', 'ng_net_set_state', 'ng_net_get_state', 'ng_net_run',
     'ng_net_run_device', 'ng_topology_create', 'ng_topology_destroy', 'ng_topology_synapses',
     'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static',
+    'ng_net_create_partitioned', 'ng_nccl_unique_id',
 )
 
 
@@ -45,7 +46,8 @@ class NetConfig(ct.Structure):
         ('t_ref_ms', ct.c_float), ('tau_exc_ms', ct.c_float), ('tau_inh_ms', ct.c_float),
         ('tau_adapt_ms', ct.c_float), ('adapt_inc_pa', ct.c_float), ('bias_pa', ct.c_float),
         ('drive_kind', ct.c_int32), ('drive_p', ct.c_float), ('drive_ns', ct.c_float),
-        ('storage', ct.c_int32), ('launch', ct.c_int32), ('reserved', ct.c_int32 * 6),
+        ('storage', ct.c_int32), ('launch', ct.c_int32), ('part_rank', ct.c_int32),
+        ('part_world', ct.c_int32), ('reserved', ct.c_int32 * 4),
     ]
 
 
@@ -125,6 +127,10 @@ def library():
     lib.ng_net_run.restype = ci
     lib.ng_net_run_device.argtypes = [vp, ci, vp, vp, vp]
     lib.ng_net_run_device.restype = ci
+    lib.ng_net_create_partitioned.argtypes = [cfgp, vp]
+    lib.ng_net_create_partitioned.restype = vp
+    lib.ng_nccl_unique_id.argtypes = [vp]
+    lib.ng_nccl_unique_id.restype = ci
     lib.ng_net_stats.argtypes = [vp, I64]
     lib.ng_net_stats.restype = ci
     lib.ng_topology_create.argtypes = [cfgp]

@@ -62,6 +62,24 @@ def scaled_262k(storage='csr', rate=0.03, seed=0):
                           storage='bsr' if storage == 'bsr' else 'csr', **common)
 
 
+def partitioned_4m(rank=0, world=1, rate=0.01, seed=0):
+    """N=4,194,304 neurons, fan-in 1,000 uniform (fp16 |N(0, 0.05)| with E/I sign), delays 1-8,
+    imposed Bernoulli(rate) spikes; rows partitioned over `world` GPUs."""
+    n = 4194304
+    return default_config(n=n, n_exc=int(n * 0.8), topology='fixed_fanin', fanin=1000,
+                          weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, delay_min=1, delay_max=8,
+                          seed=seed, drive_kind='imposed', drive_p=rate, part_rank=rank,
+                          part_world=world if world > 1 else 0)
+
+
+def nccl_unique_id():
+    """A fresh 128-byte NCCL unique id (make it on one rank, share it with the others)."""
+    buf = ct.create_string_buffer(128)
+    if library().ng_nccl_unique_id(buf):
+        raise ValueError(library().ng_error().decode())
+    return bytes(buf.raw)
+
+
 class Network:
     """One network on the current CUDA device (owns its synapses, state and stream)."""
 
@@ -78,6 +96,20 @@ class Network:
             raise ValueError(self.lib.ng_error().decode())
         self.n = cfg.n
         self.words = (self.n + 31) // 32
+
+    @classmethod
+    def partitioned(cls, cfg, nccl_id):
+        """This rank's partition (cfg.part_rank of cfg.part_world); collective over the ranks."""
+        net = cls.__new__(cls)
+        net.lib = library()
+        net.cfg = cfg
+        idbuf = ct.create_string_buffer(bytes(nccl_id), 128)
+        net.h = net.lib.ng_net_create_partitioned(ct.byref(cfg), idbuf)
+        if not net.h:
+            raise ValueError(net.lib.ng_error().decode())
+        net.n = cfg.n // cfg.part_world
+        net.words = (cfg.n + 31) // 32
+        return net
 
     def close(self):
         if getattr(self, 'h', None):

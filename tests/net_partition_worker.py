@@ -1,0 +1,57 @@
+"""Worker for tests/test_partition.py: one rank of a neuron-partitioned network.
+
+Launched as `torchrun --nproc-per-node 2 tests/net_partition_worker.py OUT`.  Every rank builds its
+partition (sharing one NCCL id through torch.distributed), runs ticks recording the whole network's
+spike bitmask, and saves its raster, counters and state slice; rank 0 also runs the unpartitioned
+network on its own GPU for comparison.
+"""
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path[:0] = [str(ROOT), str(ROOT / 'neurogen-2.5_b200')]
+
+from neurogen_b200.network import Network, default_config, nccl_unique_id  # noqa: E402
+
+
+def config(rank, world):
+    return default_config(n=65536, n_exc=52428, topology='fixed_fanin', fanin=96, weight_kind='halfnormal_f16',
+                          w_mu=0.0, w_sigma=0.05, drive_kind='conductance', drive_p=0.03, drive_ns=18.0,
+                          seed=12, part_rank=rank, part_world=world)
+
+
+def main():
+    out = Path(sys.argv[1])
+    rank, world, local = int(os.environ['RANK']), int(os.environ['WORLD_SIZE']), int(os.environ['LOCAL_RANK'])
+    torch.cuda.set_device(local)
+    import datetime
+    dist.init_process_group('gloo', timeout=datetime.timedelta(seconds=120))
+    ids = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    net = Network.partitioned(config(rank, world), ids[0])
+    spikes, counts = net.run(60)
+    net.run(100, record=False)          # graph path with the all-gather captured
+    tail, _ = net.run(5)
+    st = net.get_state()
+    np.savez(out / f'rank{rank}.npz', spikes=spikes, counts=counts, tail=tail, stats=np.array(net.stats()),
+             **{k: st[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')})
+    if rank == 0:
+        full = Network(config(0, 0))
+        fs, fc = full.run(60)
+        full.run(100, record=False)
+        ft, _ = full.run(5)
+        fst = full.get_state()
+        np.savez(out / 'full.npz', spikes=fs, counts=fc, tail=ft, stats=np.array(full.stats()),
+                 **{k: fst[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')})
+    dist.barrier()
+    net.close()
+    dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()
