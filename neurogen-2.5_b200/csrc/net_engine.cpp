@@ -400,6 +400,69 @@ void csr_from_edges(const ng_net_config &c, int64_t nnz, const int32_t *pre, con
 }
 
 // ---------------------------------------------------------------------------
+// Delay split: the synapses whose delivery the next tick waits for (delay 1)
+// go first in every row, so that the rest can be pushed while the next tick
+// already runs.  Stable within each segment.
+// ---------------------------------------------------------------------------
+void split_by_delay(HostCSR &h) {
+  const int n = h.n;
+  const bool half = !h.w16.empty();
+  std::vector<int> d1(n, 0);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; ++i) {
+    int c1 = 0;
+    for (long long e = h.row[i]; e < h.row[i] + h.outdeg[i]; ++e) c1 += (h.syn[e] >> 28) == 0;
+    d1[i] = c1;
+  }
+  std::vector<long long> row(size_t(n) + 1, 0);
+  h.mid.assign(n, 0);
+  for (int i = 0; i < n; ++i) {
+    h.mid[i] = int(pad8(d1[i]));
+    row[i + 1] = row[i] + pad8(d1[i]) + pad8(h.outdeg[i] - d1[i]);
+  }
+  const size_t total = size_t(row[n]);
+  std::vector<uint32_t> syn(total, pack_word(0, 1));
+  std::vector<uint16_t> w16(half ? total : 0, 0);
+  std::vector<float> w32(half ? 0 : total, 0.f);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; ++i) {
+    long long a = row[i], b = row[i] + h.mid[i];
+    for (long long e = h.row[i]; e < h.row[i] + h.outdeg[i]; ++e) {
+      const long long to = (h.syn[e] >> 28) == 0 ? a++ : b++;
+      syn[to] = h.syn[e];
+      if (half) w16[to] = h.w16[e];
+      else w32[to] = h.w32[e];
+    }
+  }
+  h.row.swap(row);
+  h.syn.swap(syn);
+  if (half) h.w16.swap(w16);
+  else h.w32.swap(w32);
+}
+
+void split_by_delay(HostBSR &b) {
+  b.mid.assign(b.nb, 0);
+#pragma omp parallel for schedule(static)
+  for (int bc = 0; bc < b.nb; ++bc) {
+    const long long b0 = b.bcol[bc], b1 = b.bcol[bc + 1];
+    std::vector<uint32_t> meta(b.blk.begin() + b0, b.blk.begin() + b1);
+    std::vector<uint16_t> tiles(b.tiles.begin() + b0 * 256, b.tiles.begin() + b1 * 256);
+    long long at = b0;
+    for (int pass = 0; pass < 2; ++pass)
+      for (long long k = 0; k < b1 - b0; ++k) {
+        const bool first = (meta[k] >> 28) == 0;
+        if (first != (pass == 0)) continue;
+        b.blk[at] = meta[k];
+        std::copy(tiles.begin() + k * 256, tiles.begin() + (k + 1) * 256, b.tiles.begin() + at * 256);
+        ++at;
+      }
+    int ones = 0;
+    for (uint32_t m : meta) ones += (m >> 28) == 0;
+    b.mid[bc] = ones;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host topology objects.
 // ---------------------------------------------------------------------------
 int64_t Topology::synapses() const {
@@ -443,8 +506,13 @@ Topology *make_topology(const ng_net_config &cfg) {
   auto t = std::make_unique<Topology>();
   t->cfg = cfg;
   t->blocks = cfg.storage == 1;
-  if (t->blocks) generate_bsr(cfg, t->bsr);
-  else generate_csr(cfg, t->csr);
+  if (t->blocks) {
+    generate_bsr(cfg, t->bsr);
+    split_by_delay(t->bsr);
+  } else {
+    generate_csr(cfg, t->csr);
+    split_by_delay(t->csr);
+  }
   return t.release();
 }
 
@@ -459,6 +527,7 @@ Topology *make_topology_edges(const ng_net_config &cfg, int64_t nnz, const int32
   auto t = std::make_unique<Topology>();
   t->cfg = c;
   csr_from_edges(c, nnz, pre, post, delay, w, t->csr);
+  split_by_delay(t->csr);
   return t.release();
 }
 
@@ -502,10 +571,13 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
     blk_ = upload_vec(bsr->blk);
     tiles_ = upload_vec(bsr->tiles);
     outdeg_ = upload_vec(bsr->outdeg);
+    if (int(bsr->mid.size()) != bsr->nb) throw std::logic_error("block-columns not split by delay");
+    mid_ = upload_vec(bsr->mid);
     d.bsr = 1;
     d.bcol = bcol_.as<long long>();
     d.blk = blk_.as<uint32_t>();
     d.tiles = tiles_.as<uint16_t>();
+    d.bmid = mid_.as<int>();
     for (int x : bsr->outdeg) nnz_ += x;
   } else {
     row_ = upload_vec(csr->row);
@@ -518,9 +590,12 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
       w_ = upload_padded(csr->w32, kTailPad);
       d.w_half = 0;
     }
+    if (int(csr->mid.size()) != csr->n) throw std::logic_error("CSR rows not split by delay");
+    mid_ = upload_vec(csr->mid);
     d.row = row_.as<long long>();
     d.syn = syn_.as<uint32_t>();
     d.w = w_.as<void>();
+    d.mid = mid_.as<int>();
     for (int x : csr->outdeg) nnz_ += x;
   }
   d.outdeg = outdeg_.as<int>();
@@ -563,18 +638,21 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
   d.drive_thr = thr >= 4294967295.0 ? 0xFFFFFFFFu : uint32_t(thr);
   d.drive_key = mix64(c.seed ^ 0xD41Eull);
   d.ref_ticks = int(std::lround(double(c.t_ref_ms) / double(c.dt_ms)));
-  // Whole-network bitmask (padded to whole 256-neuron groups), per-group
-  // totals (enough pairs for the held groups and the presynaptic groups), tick.
+  // Whole-network bitmask (padded to whole 256-neuron groups) twice, for
+  // even and odd ticks; per-group counters (enough for the held groups and
+  // the presynaptic groups); tick.
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
   const size_t groups = std::max(pre_groups, (N + kNetBlock - 1) / kNetBlock);
-  bitmask_.reset(pre_groups * (kNetBlock / 32) * 4);
-  totals_.reset(groups * 2 * sizeof(unsigned long long));
+  const size_t bm_words = pre_groups * (kNetBlock / 32);
+  bitmask_.reset(2 * bm_words * 4);
+  totals_.reset(groups * kTotalsStride * sizeof(unsigned long long));
   tick_dev_.reset(sizeof(long long));
-  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, pre_groups * (kNetBlock / 32) * 4));
-  NGB_CUDA(cudaMemset(totals_.as<void>(), 0, groups * 2 * sizeof(unsigned long long)));
+  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, 2 * bm_words * 4));
+  NGB_CUDA(cudaMemset(totals_.as<void>(), 0, groups * kTotalsStride * sizeof(unsigned long long)));
   totals_pairs_ = groups;
   NGB_CUDA(cudaMemset(tick_dev_.as<void>(), 0, sizeof(long long)));
   d.bitmask = bitmask_.as<uint32_t>();
+  d.bm_stride = int(bm_words);
   d.totals = totals_.as<unsigned long long>();
   // Small networks: one fused launch per tick; large or partitioned: split
   // membrane / push, with the bitmask all-gather between them.
@@ -591,35 +669,81 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
 Network::~Network() {
   if (graph_) cudaGraphExecDestroy(graph_); // before the communicator its NCCL nodes use
   if (comm_) nccl().CommDestroy(comm_);
+  for (cudaEvent_t e : {ev_fork_, ev_alif_, ev_rest_[0], ev_rest_[1], ev_join_})
+    if (e) cudaEventDestroy(e);
+  if (stream_rest_) cudaStreamDestroy(stream_rest_);
   if (stream) cudaStreamDestroy(stream);
 }
 
-void Network::launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st) {
+// Membrane update of tick t (parity = t & 1, known on the host) and, for a
+// partitioned network, the all-gather of the held slice of that tick's
+// bitmask buffer into every rank's copy of the whole bitmask.
+void Network::launch_membrane(TickRef t, int parity, uint32_t *spikes_row, unsigned long long *counts_row,
+                              cudaStream_t st) {
+  launch_net_alif(dev_, t, world_ > 1 ? nullptr : spikes_row, counts_row, st);
   if (world_ > 1) {
-    // Held slice of the bitmask -> every rank's copy of the whole bitmask.
+    uint32_t *bm = bitmask_.as<uint32_t>() + size_t(parity) * size_t(dev_.bm_stride);
     const size_t words = size_t(n_) / 32;
-    launch_net_alif(dev_, t, nullptr, counts_row, st);
-    uint32_t *bm = bitmask_.as<uint32_t>();
     nccl_check(nccl().AllGather(bm + size_t(base_) / 32, bm, words, ncclUint32, comm_, st), "ncclAllGather");
     if (spikes_row)
       NGB_CUDA(cudaMemcpyAsync(spikes_row, bm, size_t(n_pre_) / 32 * 4, cudaMemcpyDeviceToDevice, st));
-    launch_net_push(dev_, t, counts_row, st);
-  } else if (split_) {
-    launch_net_alif(dev_, t, spikes_row, counts_row, st);
-    launch_net_push(dev_, t, counts_row, st);
+  }
+}
+
+// One whole tick in order on one stream (recorded runs, the ticks outside
+// whole graph replays).
+void Network::launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned long long *counts_row,
+                          cudaStream_t st) {
+  if (split_) {
+    launch_membrane(t, parity, spikes_row, counts_row, st);
+    launch_net_push(dev_, t, counts_row, 0, st);
   } else {
     launch_net_fused(dev_, t, spikes_row, counts_row, st);
   }
 }
 
 // One CUDA graph of kGraphTicks ticks reading the tick number from a device
-// counter (advanced by the graph's last node), so it can be replayed for any
-// starting tick.
+// counter (advanced by the graph's last node); replays start on even ticks.
+// Split networks run pipelined over two streams.  The membrane update and
+// the delay-1 push of tick t stay on the main stream, since tick t+1 reads
+// what they write.  The delay>=2 push of tick t runs on a second stream
+// beside tick t+1: it writes ring slots t+2.. only, and its own counter
+// slot.  Tick t+2's membrane update waits for it, because that tick reads
+// ring slot t+2 and rewrites tick t's bitmask buffer.
 void Network::capture_graph() {
+  const long long *td = tick_dev_.as<long long>();
+  if (split_ && !stream_rest_) {
+    NGB_CUDA(cudaStreamCreateWithFlags(&stream_rest_, cudaStreamNonBlocking));
+    for (cudaEvent_t *e : {&ev_fork_, &ev_alif_, &ev_rest_[0], &ev_rest_[1], &ev_join_})
+      NGB_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  }
   cudaGraph_t g = nullptr;
   NGB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-  for (int k = 0; k < kGraphTicks; ++k) launch_tick(TickRef{tick_dev_.as<long long>(), k}, nullptr, nullptr, stream);
-  launch_add_tick(tick_dev_.as<long long>(), kGraphTicks, stream);
+  try {
+    if (split_) {
+      NGB_CUDA(cudaEventRecord(ev_fork_, stream));
+      NGB_CUDA(cudaStreamWaitEvent(stream_rest_, ev_fork_, 0));
+      for (int k = 0; k < kGraphTicks; ++k) {
+        const TickRef t{td, k};
+        if (k >= 2) NGB_CUDA(cudaStreamWaitEvent(stream, ev_rest_[k & 1], 0));
+        launch_membrane(t, k & 1, nullptr, nullptr, stream);
+        NGB_CUDA(cudaEventRecord(ev_alif_, stream));
+        launch_net_push(dev_, t, nullptr, 1, stream);
+        NGB_CUDA(cudaStreamWaitEvent(stream_rest_, ev_alif_, 0));
+        launch_net_push(dev_, t, nullptr, 2, stream_rest_);
+        NGB_CUDA(cudaEventRecord(ev_rest_[k & 1], stream_rest_));
+      }
+      NGB_CUDA(cudaEventRecord(ev_join_, stream_rest_));
+      NGB_CUDA(cudaStreamWaitEvent(stream, ev_join_, 0));
+    } else {
+      for (int k = 0; k < kGraphTicks; ++k) launch_tick(TickRef{td, k}, k & 1, nullptr, nullptr, stream);
+    }
+    launch_add_tick(tick_dev_.as<long long>(), kGraphTicks, stream);
+  } catch (...) {
+    cudaStreamEndCapture(stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
   const cudaError_t e = cudaStreamEndCapture(stream, &g);
   if (e != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
@@ -634,12 +758,12 @@ void Network::stats(int64_t *totals) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaDeviceSynchronize());
   const size_t groups = totals_pairs_;
-  std::vector<unsigned long long> g(groups * 2);
+  std::vector<unsigned long long> g(groups * kTotalsStride);
   NGB_CUDA(cudaMemcpy(g.data(), totals_.as<void>(), g.size() * 8, cudaMemcpyDeviceToHost));
   totals[0] = totals[1] = 0;
   for (size_t k = 0; k < groups; ++k) {
-    totals[0] += int64_t(g[2 * k]);
-    totals[1] += int64_t(g[2 * k + 1]);
+    totals[0] += int64_t(g[kTotalsStride * k]);
+    totals[1] += int64_t(g[kTotalsStride * k + 1]) + int64_t(g[kTotalsStride * k + 2]);
   }
 }
 
@@ -713,14 +837,19 @@ void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_count
   const size_t words = (size_t(n_pre_) + 31) / 32;
   if (d_counts) NGB_CUDA(cudaMemsetAsync(d_counts, 0, size_t(ticks) * 16, st));
   int k = 0;
-  if (!d_spikes && !d_counts && ticks >= kGraphTicks) {
+  auto direct = [&](int kk) {
+    const long long t = tick_ + kk;
+    launch_tick(TickRef{nullptr, t}, int(t & 1), d_spikes ? d_spikes + size_t(kk) * words : nullptr,
+                d_counts ? d_counts + 2 * size_t(kk) : nullptr, st);
+  };
+  const int lead = int(tick_ & 1); // graph replays start on even ticks
+  if (!d_spikes && !d_counts && ticks - lead >= kGraphTicks) {
+    if (lead) direct(k++);
     if (!graph_) capture_graph();
-    launch_set_tick(tick_dev_.as<long long>(), tick_, st);
+    launch_set_tick(tick_dev_.as<long long>(), tick_ + k, st);
     for (; k + kGraphTicks <= ticks; k += kGraphTicks) NGB_CUDA(cudaGraphLaunch(graph_, st));
   }
-  for (; k < ticks; ++k)
-    launch_tick(TickRef{nullptr, tick_ + k}, d_spikes ? d_spikes + size_t(k) * words : nullptr,
-                d_counts ? d_counts + 2 * size_t(k) : nullptr, st);
+  for (; k < ticks; ++k) direct(k);
   NGB_CUDA(cudaGetLastError());
   tick_ += ticks;
 }

@@ -21,6 +21,9 @@ struct HostCSR {
   std::vector<float> w32;        // signed weights (fp32 storage), or
   std::vector<uint16_t> w16;     // fp16 bits (fp16 storage)
   std::vector<int> outdeg;       // non-zero synapses per row
+  // Offset (from the row start, a multiple of 8) of the row's second segment:
+  // rows hold their delay-1 synapses first, then the rest, each segment padded.
+  std::vector<int> mid;
 };
 
 // 16x16 blocks by block-column, host form.
@@ -30,7 +33,13 @@ struct HostBSR {
   std::vector<uint32_t> blk;     // block-row | (delay-1) << 28
   std::vector<uint16_t> tiles;   // fp16 [block][16 columns][16 rows]
   std::vector<int> outdeg;       // non-zero synapses per presynaptic neuron
+  std::vector<int> mid;          // per block-column: number of its delay-1 blocks (listed first)
 };
+
+// Reorders each CSR row (block-column) so that its delay-1 synapses (blocks)
+// come first, in their own padded segment; fills `mid`.
+void split_by_delay(HostCSR &h);
+void split_by_delay(HostBSR &b);
 
 // A generated or caller-given synapse set on the host (no device needed).
 struct Topology {
@@ -86,14 +95,18 @@ private:
   int64_t nnz_ = 0;
   long long tick_ = 0;
   NetDev dev_{};
-  DeviceBuffer row_, syn_, w_, outdeg_, bcol_, blk_, tiles_;
+  DeviceBuffer row_, syn_, w_, outdeg_, mid_, bcol_, blk_, tiles_;
   DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
   DeviceBuffer rec_spikes_, rec_counts_;
   DeviceBuffer bitmask_, totals_, tick_dev_;
   bool split_ = false;
   cudaGraphExec_t graph_ = nullptr;
   static constexpr int kGraphTicks = 64;
-  void launch_tick(TickRef t, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st);
+  cudaStream_t stream_rest_ = nullptr; // graph replays: delay>=2 pushes beside the next tick
+  cudaEvent_t ev_fork_ = nullptr, ev_alif_ = nullptr, ev_rest_[2] = {nullptr, nullptr}, ev_join_ = nullptr;
+  void launch_membrane(TickRef t, int parity, uint32_t *spikes_row, unsigned long long *counts_row,
+                       cudaStream_t st);
+  void launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st);
   void capture_graph();
 };
 

@@ -107,12 +107,13 @@ __device__ __forceinline__ bool alif_update(const NetDev &d, long long t, int i)
 // Fixed-point amount (2^-24 nS units) of a signed weight.
 __device__ __forceinline__ int quantum(float w) { return __float2int_rn(__fmul_rn(fabsf(w), 16777216.f)); }
 
-__device__ __forceinline__ void deliver(const NetDev &d, long long t, uint32_t word, float w) {
-  if (w == 0.f) return;
+__device__ __forceinline__ int deliver(const NetDev &d, long long t, uint32_t word, float w) {
+  if (w == 0.f) return 0;
   const int post = (int)(word & kPostMask);
   const int dly = (int)(word >> 28) + 1;
   const int slot = (int)((t + dly) & (kRingSlots - 1));
   atomicAdd(reinterpret_cast<int *>(d.ring) + ((size_t)slot * d.n + post) * 2 + (w < 0.f ? 1 : 0), quantum(w));
+  return 1;
 }
 
 __device__ __forceinline__ float half_bits(uint32_t bits16) {
@@ -125,8 +126,13 @@ __device__ __forceinline__ float half_bits(uint32_t bits16) {
 // caches (evict-first) before any delivery.  Rows are padded to multiples of
 // 8 and the arrays carry 16 spare entries, so the loads stay in bounds; the
 // deliveries are masked to the row.
-__device__ __forceinline__ void push_row(const NetDev &d, long long t, int pre, int lane) {
-  const long long e0 = d.row[pre], e1 = d.row[pre + 1];
+// seg selects the whole row (0), its delay-1 segment (1) or the rest (2).
+// Returns this lane's delivered (non-zero) synapse count.
+__device__ __forceinline__ int push_row(const NetDev &d, long long t, int pre, int lane, int seg) {
+  long long e0 = d.row[pre], e1 = d.row[pre + 1];
+  if (seg == 1) e1 = e0 + d.mid[pre];
+  else if (seg == 2) e0 += d.mid[pre];
+  int delivered = 0;
   for (long long e = e0 + lane * 16; e < e1; e += 512) {
     const uint4 *ps = reinterpret_cast<const uint4 *>(d.syn + e);
     uint4 p[4];
@@ -154,15 +160,20 @@ __device__ __forceinline__ void push_row(const NetDev &d, long long t, int pre, 
                                p[2].x, p[2].y, p[2].z, p[2].w, p[3].x, p[3].y, p[3].z, p[3].w};
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      if (e + j < e1) deliver(d, t, word[j], w[j]);
+      if (e + j < e1) delivered += deliver(d, t, word[j], w[j]);
   }
+  return delivered;
 }
 
 // Push the spiking columns `sub` (16-bit mask) of block-column bc: each lane
 // takes one block at a time, sums the selected tile columns per post row in
 // fixed point (E and I apart), and issues one atomic per non-zero row sum.
-__device__ __forceinline__ void push_block_column(const NetDev &d, long long t, int bc, unsigned sub, int lane) {
-  const long long b0 = d.bcol[bc], b1 = d.bcol[bc + 1];
+__device__ __forceinline__ int push_block_column(const NetDev &d, long long t, int bc, unsigned sub, int lane,
+                                                 int seg) {
+  long long b0 = d.bcol[bc], b1 = d.bcol[bc + 1];
+  if (seg == 1) b1 = b0 + d.bmid[bc];
+  else if (seg == 2) b0 += d.bmid[bc];
+  int delivered = 0;
   for (long long b = b0 + lane; b < b1; b += 32) {
     const uint32_t meta = __ldcs(d.blk + b);
     const int br = (int)(meta & kPostMask);
@@ -183,6 +194,7 @@ __device__ __forceinline__ void push_block_column(const NetDev &d, long long t, 
         for (int q = 0; q < 2; ++q) {
           const float w = half_bits(q ? h[j] >> 16 : h[j] & 0xFFFFu);
           const int amount = w == 0.f ? 0 : quantum(w);
+          delivered += w != 0.f;
           if (w < 0.f) acc[1][2 * j + q] += amount;
           else acc[0][2 * j + q] += amount;
         }
@@ -196,6 +208,7 @@ __device__ __forceinline__ void push_block_column(const NetDev &d, long long t, 
       if (acc[1][r]) atomicAdd(ring + 2 * r + 1, acc[1][r]);
     }
   }
+  return delivered;
 }
 
 // CTA-wide sum of one value per warp (lane 0 contributes), added to this
@@ -228,7 +241,7 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane; // fused launches are unpartitioned: base 0
   if (lane == 0 && base < d.n) {
-    d.bitmask[base >> 5] = fired;
+    d.bitmask[(t & 1) * d.bm_stride + (base >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   unsigned long long events = 0;
@@ -236,18 +249,17 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const unsigned sub = (fired >> (16 * half)) & 0xFFFFu;
-      if (sub) push_block_column(d, t, (base >> 4) + half, sub, lane);
+      if (sub) events += push_block_column(d, t, (base >> 4) + half, sub, lane, 0);
     }
   } else {
     unsigned m = fired;
     while (m) {
       const int src = __ffs(m) - 1;
       m &= m - 1;
-      push_row(d, t, base + src, lane);
+      events += push_row(d, t, base + src, lane, 0);
     }
   }
-  if (s) events = (unsigned long long)d.outdeg[i];
-  unsigned long long *group = d.totals + 2 * (size_t)blockIdx.x;
+  unsigned long long *group = d.totals + kTotalsStride * (size_t)blockIdx.x;
   add_block_count(lane == 0 ? __popc(fired) : 0, group, counts);
   add_block_count(events, group + 1, counts ? counts + 1 : nullptr);
 }
@@ -262,25 +274,27 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
   if (lane == 0 && base < d.n) {
-    d.bitmask[(d.base + base) >> 5] = fired;
+    d.bitmask[(t & 1) * d.bm_stride + ((d.base + base) >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
-  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + 2 * (size_t)blockIdx.x, counts);
+  add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + kTotalsStride * (size_t)blockIdx.x, counts);
 }
 
 // CTA b pushes the spikes of neurons [256b, 256b+256): its warps list them
-// from the group's 8 bitmask words and take them round-robin.
-template <bool BSR>
+// from the group's 8 bitmask words and take them round-robin.  SEG selects
+// whole rows (0), delay-1 segments (1) or delay>=2 segments (2).
+template <bool BSR, int SEG>
 __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned long long *counts) {
   __shared__ int items[TB];
   __shared__ unsigned item_mask[TB / 16];
   __shared__ int n_items;
   const long long t = tick_of(tr);
+  const uint32_t *bitmask = d.bitmask + (t & 1) * d.bm_stride;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int base = blockIdx.x * TB;
   if (warp == 0) {
     const int w = base / 32 + (lane & 7);
-    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n_pre) ? d.bitmask[w] : 0u;
+    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n_pre) ? bitmask[w] : 0u;
     if (BSR) {
       // 16 block-columns per group; lane k < 16 owns half (k & 1) of word k / 2.
       const unsigned wk = __shfl_sync(0xffffffffu, word, (lane >> 1) & 7);
@@ -315,18 +329,11 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
   const int count = n_items;
   unsigned long long events = 0;
   for (int k = warp; k < count; k += WARPS) {
-    if (BSR) {
-      const int bc = items[k];
-      const unsigned sub = item_mask[k];
-      push_block_column(d, t, bc, sub, lane);
-      if (lane < 16 && (sub >> lane & 1u)) events += (unsigned long long)d.outdeg[bc * 16 + lane];
-    } else {
-      const int pre = items[k];
-      push_row(d, t, pre, lane);
-      if (lane == 0) events += (unsigned long long)d.outdeg[pre];
-    }
+    if (BSR) events += push_block_column(d, t, items[k], item_mask[k], lane, SEG);
+    else events += push_row(d, t, items[k], lane, SEG);
   }
-  add_block_count(events, d.totals + 2 * (size_t)blockIdx.x + 1, counts ? counts + 1 : nullptr);
+  add_block_count(events, d.totals + kTotalsStride * (size_t)blockIdx.x + (SEG == 2 ? 2 : 1),
+                  counts ? counts + 1 : nullptr);
 }
 
 __global__ void k_set_tick(long long *t, long long v) { *t = v; }
@@ -348,10 +355,17 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
   else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
 }
 
-void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, cudaStream_t s) {
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s) {
   const int blocks = (d.n_pre + TB - 1) / TB;
-  if (d.bsr) k_net_push<true><<<blocks, TB, 0, s>>>(d, t, counts);
-  else k_net_push<false><<<blocks, TB, 0, s>>>(d, t, counts);
+  if (d.bsr) {
+    if (seg == 1) k_net_push<true, 1><<<blocks, TB, 0, s>>>(d, t, counts);
+    else if (seg == 2) k_net_push<true, 2><<<blocks, TB, 0, s>>>(d, t, counts);
+    else k_net_push<true, 0><<<blocks, TB, 0, s>>>(d, t, counts);
+  } else {
+    if (seg == 1) k_net_push<false, 1><<<blocks, TB, 0, s>>>(d, t, counts);
+    else if (seg == 2) k_net_push<false, 2><<<blocks, TB, 0, s>>>(d, t, counts);
+    else k_net_push<false, 0><<<blocks, TB, 0, s>>>(d, t, counts);
+  }
 }
 
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s) { k_set_tick<<<1, 1, 0, s>>>(t_dev, value); }

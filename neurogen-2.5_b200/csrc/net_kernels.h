@@ -23,19 +23,23 @@ struct NetDev {
   const void *w;        // fp16 or fp32 signed weights (nS; negative = inhibitory)
   int w_half;
   const int *outdeg; // non-zero synapses per presynaptic neuron
+  const int *mid;    // per row: offset of its delay>=2 segment (delay-1 synapses first)
   // 16x16 block storage by block-column (pre block), blocks sorted by block-row.
   int bsr;
   const long long *bcol; // [n/16+1]
   const uint32_t *blk;   // block-row | (delay-1) << 28
   const uint16_t *tiles; // fp16 [block][16 pre columns][16 post rows]
+  const int *bmid;       // per block-column: number of its delay-1 blocks (first)
   // State (fp32 SoA) and the E/I delay ring [16][n] of int2 (E, I) in 2^-24 nS.
   float *v, *a, *ge, *gi;
   int *ref;
   int2 *ring;
-  uint32_t *bitmask;            // this tick's spike words of the whole network [ceil(n_pre/32)]
-  // Running counters since creation, one pair per 256-neuron group: [g][0]
+  uint32_t *bitmask;            // spike words of the whole network, two buffers (tick parity)
+  int bm_stride;                // words per buffer
+  // Running counters since creation, three per 256-neuron group: [g][0]
   // spikes of held group g (membrane kernel), [g][1] events pushed from
-  // presynaptic group g (push kernel).  One writer per entry, no atomics.
+  // presynaptic group g by the delay-1 (or whole-row) push, [g][2] by the
+  // delay>=2 push.  One writer per entry, no atomics.
   unsigned long long *totals;
   // Constants (see net_kernels.cu for the exact operation order).
   float dE, dI, dA, g_leak, gLEL, e_inh, v_th, v_reset, cap_e, cap_i, neg_dt, adapt_inc, bias,
@@ -60,7 +64,9 @@ void launch_net_fused(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned
 // each 256-neuron group by one CTA.
 void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
                      cudaStream_t s);
-void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, cudaStream_t s);
+// seg: 0 whole rows, 1 delay-1 segments only, 2 delay>=2 segments only.
+void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s);
+constexpr int kTotalsStride = 3;
 constexpr int kNetBlock = 256; // neurons per membrane CTA
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s);
 void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s);
