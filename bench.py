@@ -180,20 +180,33 @@ def tick_config(name, rate, rank=0, world=1):
 
 
 def tick_bytes(cfg, spikes, events, held=None):
-    """Algorithmic DRAM bytes of one tick (roofline section).
+    """Algorithmic DRAM bytes of one tick, the roofline numerator.
 
-    Per neuron: V, adaptation, g_E, g_I (fp32) and refractory (int32) read and written (40 B),
-    its ring slot (int2) read and cleared (16 B).  Per spiking neuron: its row bounds and
-    synapse count (20 B).  Per delivered synapse: the packed post/delay word and the weight.
+    Per neuron: the four fp32 state values (V, adaptation, g_E, g_I) read and written (32 B),
+    its ring slot read and cleared (16 B) and its spike bit (1/8 B).  Per delivered synapse
+    (CSR): a 4-byte index, the weight (2 B fp16 or 4 B fp32) and a 1-byte delay.  Block
+    storage: per spiking neuron and block of its block-column, the 32-byte tile column plus
+    the block's 4-byte row/delay word.
     """
     wbytes = 2 if cfg.weight_kind == 1 else 4
     held = cfg.n if held is None else held
+    per_neuron = held * 48 + held / 8
     if cfg.storage == 1:
-        # Block storage: per spiking neuron and block of its block-column, one 32-byte tile
-        # column plus the block's 4-byte row/delay word; events counted per non-zero.
-        blocks_per_col = cfg.bsr_blocks
-        return held * 56 + spikes * (16 + blocks_per_col * 36)
-    return held * 56 + spikes * 20 + events * (4 + wbytes)
+        return per_neuron + spikes * cfg.bsr_blocks * 36
+    return per_neuron + events * (4 + wbytes + 1)
+
+
+KERNEL_OF_LAUNCH = {'fused': 'k_net_fused', 'split': 'tick = k_net_alif + k_net_push',
+                    'resident': 'k_net_resident (persistent, 2,048 ticks a launch)'}
+
+
+def tick_launches(mode, ticks):
+    """Kernels the engine launches for one run of `ticks` ticks without per-tick outputs."""
+    if mode == 'resident':
+        return -(-ticks // 2048)
+    per_tick = 1 if mode == 'fused' else (3 if mode == 'split' else 1)
+    graphs = ticks // 64
+    return graphs * (64 * per_tick + 1) + (ticks - graphs * 64) * per_tick + (1 if graphs else 0)
 
 
 def bench_ticks(args, dist):
@@ -217,7 +230,7 @@ def bench_ticks(args, dist):
         net = topo.network()
         synapses = topo.synapses
     setup_s = time.time() - t0
-    split = part or cfg.launch == 2 or (cfg.launch == 0 and cfg.n >= 65536)
+    mode = net.launch  # 'fused', 'split' or 'resident'
     stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
@@ -260,13 +273,12 @@ def bench_ticks(args, dist):
                    'l2': 'inputs larger than L2' if synapses * 6 > 126e6 else 'network fits in L2',
                    'parallelism': (f'rows{dist.world} + NCCL bitmask all-gather' if part and dist.world > 1
                                    else f'replicas{dist.world}'),
-                   'setup_s': round(setup_s, 2)},
+                   'launch': mode, 'setup_s': round(setup_s, 2)},
         'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
                      'frac': achieved / peak_total, 'traffic': None, 'bytes_per_tick': b_tick,
-                     'kernel': 'tick = k_net_alif + k_net_push' if split else 'k_net_fused',
-                     'peak_source': src},
-        'gpu_launches': total_ticks * (2 if split else 1) + args.steps * (-(-ticks // 64) + 1),
+                     'kernel': KERNEL_OF_LAUNCH[mode], 'peak_source': src},
+        'gpu_launches': tick_launches(mode, ticks) * args.steps,
         'clocks': clk.summary(),
     }
     if not args.no_e2e:

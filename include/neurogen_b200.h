@@ -163,7 +163,12 @@ typedef struct {
   float drive_ns;               /* conductance added per drive event */
   int32_t storage;              /* 0 = CSR push, 1 = BSR push (BSR16 topology) */
   int32_t launch;               /* 0 = auto, 1 = one fused launch per tick,
-                                   2 = split membrane / push launches            */
+                                   2 = split membrane / push launches,
+                                   3 = resident: one persistent launch runs many
+                                   ticks with neuron state and delay ring in
+                                   shared memory (CSR storage, unpartitioned).
+                                   Auto picks 3 when the network fits, else 1
+                                   below 65,536 neurons, else 2.                */
   int32_t part_rank, part_world; /* neuron row-partition: this rank owns neurons
                                    [rank*n/world, (rank+1)*n/world); 0/1 = whole */
   int32_t reserved[4];
@@ -211,6 +216,11 @@ void *ng_net_create_topology(const void *topology);
  * pre-major (arrays sized ng_net_synapses).  For a partitioned network: this
  * rank's synapses, with global neuron indices. */
 int64_t ng_net_synapses(void *net);
+
+/* Launch shape the network runs with: 1 fused, 2 split, 3 resident; -1 on a
+ * null handle.  No counterpart in the reference (its isolated-tick network is
+ * biology.py's NumPy loop). */
+int ng_net_launch_kind(void *net);
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay,
                   float *weight);
 

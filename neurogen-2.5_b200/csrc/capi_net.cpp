@@ -120,6 +120,12 @@ void ng_net_destroy(void *net) { delete static_cast<Network *>(net); }
 
 int64_t ng_net_synapses(void *net) { return net ? static_cast<Network *>(net)->synapses() : -1; }
 
+int ng_net_launch_kind(void *net) {
+  if (!net) return -1;
+  const Network &w = *static_cast<Network *>(net);
+  return w.resident() ? 3 : w.split() ? 2 : 1;
+}
+
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay, float *weight) {
   return guarded([&] {
     if (!net) throw std::invalid_argument("Null network");

@@ -1,7 +1,7 @@
 // Isolated-tick spiking network: seeded topology generation, CSR / 16x16-block
 // layouts by presynaptic neuron, device state and the tick loop.
 //
-// Generated inputs (3, 5) are deterministic functions of
+// Generated networks (Erdos-Renyi, fixed fan-in, 16x16 blocks) are deterministic functions of
 // the seed through a counter-based generator (splitmix64 of (stream, a, b)),
 // so any machine and any thread count produce the same network.  Weights are
 // rounded onto the delay ring's fixed-point grid (multiples of 2^-24 nS):
@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -116,7 +117,10 @@ void validate_config(const ng_net_config &c) {
     throw std::invalid_argument("Unknown drive kind");
   if (c.drive_p < 0 || c.drive_p > 1) throw std::invalid_argument("drive_p must be in [0, 1]");
   if (c.storage != 0 && c.storage != 1) throw std::invalid_argument("storage must be 0 (CSR) or 1 (BSR)");
-  if (c.launch < 0 || c.launch > 2) throw std::invalid_argument("launch must be 0 (auto), 1 (fused) or 2 (split)");
+  if (c.launch < 0 || c.launch > 3)
+    throw std::invalid_argument("launch must be 0 (auto), 1 (fused), 2 (split) or 3 (resident)");
+  if (c.launch == 3 && (c.storage != 0 || c.part_world > 1))
+    throw std::invalid_argument("The resident launch needs CSR storage and an unpartitioned network");
   switch (c.topology) {
   case NG_TOPO_ERDOS_RENYI:
     if (!(c.p_connect >= 0 && c.p_connect <= 1)) throw std::invalid_argument("p_connect must be in [0, 1]");
@@ -641,8 +645,11 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
   // Whole-network bitmask (padded to whole 256-neuron groups) twice, for
   // even and odd ticks; per-group counters (enough for the held groups and
   // the presynaptic groups); tick.
+  // Resident launch (persistent kernel, state in shared memory) when asked
+  // for, or by default when the network qualifies and fits.
+  if (csr && world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(*csr, c.launch == 3);
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
-  const size_t groups = std::max(pre_groups, (N + kNetBlock - 1) / kNetBlock);
+  const size_t groups = std::max({pre_groups, (N + kNetBlock - 1) / kNetBlock, size_t(resident_ ? res_.ctas : 0)});
   const size_t bm_words = pre_groups * (kNetBlock / 32);
   bitmask_.reset(2 * bm_words * 4);
   totals_.reset(groups * kTotalsStride * sizeof(unsigned long long));
@@ -664,6 +671,93 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
     nccl_check(nccl().CommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
   }
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  if (resident_) build_owner_blocks();
+}
+
+// Resident launch plan: CTAs of P neurons (a multiple of 32, at least 256 so
+// that small networks use few CTAs), one CTA per SM at most, shared memory for
+// the state, a ring of Dr slots and the warps' event staging.  Returns false
+// (or throws, when the resident launch was asked for) if it does not fit.
+bool Network::plan_resident(const HostCSR &h, bool required) {
+  auto fail = [&](const std::string &why) -> bool {
+    if (required) throw std::invalid_argument("Resident launch unavailable: " + why);
+    return false;
+  };
+  int coop = 0, sms = 0, optin = 0;
+  NGB_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+  NGB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  NGB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  if (!coop) return fail("the device has no cooperative launch");
+  int max_delay = 1;
+  for (uint32_t w : h.syn) max_delay = std::max(max_delay, int(w >> 28) + 1);
+  int dr = 1;
+  while (dr < max_delay) dr <<= 1;
+  const bool ev64 = dev_.w_half == 0;
+  int P = ((n_ + sms - 1) / sms + 31) / 32 * 32;
+  P = std::max(P, std::min(256, (n_ + 31) / 32 * 32));
+  if (const char *env = std::getenv("NEUROGEN_RESIDENT_PER_CTA")) P = std::max(P, (std::atoi(env) + 31) / 32 * 32);
+  if (P > 2048) return fail("more than 2048 neurons per CTA (" + std::to_string(n_) + " neurons, " +
+                            std::to_string(sms) + " SMs)");
+  ResidentDev r{};
+  r.per_cta = P;
+  r.ctas = (n_ + P - 1) / P;
+  r.ring_depth = dr;
+  r.ev64 = ev64 ? 1 : 0;
+  if (!ev64 && 2 * (dr + 1) * P >= 65536) return fail("ring offsets of " + std::to_string(P) + " neurons do not fit 16 bits");
+  const size_t smem = resident_smem_bytes(r);
+  if (smem + 2048 > size_t(optin)) // static shared memory and slack
+    return fail(std::to_string(P) + " neurons a CTA with a " + std::to_string(dr) +
+                "-slot ring need more shared memory than a CTA has");
+  if (resident_max_ctas(ev64, smem) < r.ctas)
+    return fail("the device cannot hold " + std::to_string(r.ctas) + " resident CTAs at once");
+  res_ = r;
+  return true;
+}
+
+// Owner blocks from the device CSR: count the overflow blocks, allocate
+// exactly, fill.
+void Network::build_owner_blocks() {
+  ResidentDev &r = res_;
+  const size_t C = size_t(r.ctas);
+  res_lists_.reset(2 * size_t(n_pre_) * 4);
+  res_sync_.reset(16);
+  res_err_.reset(4);
+  NGB_CUDA(cudaMemset(res_sync_.as<void>(), 0, 16));
+  NGB_CUDA(cudaMemset(res_err_.as<void>(), 0, 4));
+  r.lists = res_lists_.as<int>();
+  r.sync = res_sync_.as<unsigned>();
+  r.err = res_err_.as<int>();
+  DeviceBuffer scratch(16);
+  unsigned long long *need = scratch.as<unsigned long long>(), *cursor = need + 1;
+  NGB_CUDA(cudaMemsetAsync(need, 0, 16, stream));
+  launch_owner_count(dev_, r, need, stream);
+  NGB_CUDA(cudaGetLastError());
+  unsigned long long overflow = 0;
+  NGB_CUDA(cudaMemcpyAsync(&overflow, need, 8, cudaMemcpyDeviceToHost, stream));
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  const unsigned long long total = (unsigned long long)n_pre_ * C + overflow;
+  if (!r.ev64 && total >= 0x7FFFFFFFull) throw std::invalid_argument("Too many owner blocks for 32-bit events");
+  const size_t bytes = size_t(total) * kOwnerBlockSlots * (r.ev64 ? 8 : 4);
+  res_blocks_.reset(bytes);
+  NGB_CUDA(cudaMemsetAsync(res_blocks_.as<void>(), 0xFF, bytes, stream));
+  launch_owner_fill(dev_, r, res_blocks_.as<void>(), cursor, overflow, r.err, stream);
+  NGB_CUDA(cudaGetLastError());
+  int err = 0;
+  unsigned long long used = 0;
+  NGB_CUDA(cudaMemcpyAsync(&err, r.err, 4, cudaMemcpyDeviceToHost, stream));
+  NGB_CUDA(cudaMemcpyAsync(&used, cursor, 8, cudaMemcpyDeviceToHost, stream));
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  if (err || used != overflow) throw std::logic_error("Owner-block construction overflowed its allocation");
+  r.blocks = res_blocks_.as<void>();
+}
+
+// Raises the resident kernel's error (a grid barrier that timed out).
+void Network::check_resident() {
+  if (!resident_) return;
+  int err = 0;
+  NGB_CUDA(cudaMemcpy(&err, res_.err, 4, cudaMemcpyDeviceToHost));
+  if (err)
+    throw std::runtime_error("Resident tick kernel: a grid barrier wait timed out; the network state is undefined");
 }
 
 Network::~Network() {
@@ -757,6 +851,7 @@ void Network::capture_graph() {
 void Network::stats(int64_t *totals) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaDeviceSynchronize());
+  check_resident();
   const size_t groups = totals_pairs_;
   std::vector<unsigned long long> g(groups * kTotalsStride);
   NGB_CUDA(cudaMemcpy(g.data(), totals_.as<void>(), g.size() * 8, cudaMemcpyDeviceToHost));
@@ -822,6 +917,7 @@ void Network::set_state(const float *v, const float *a, const float *ge, const f
 void Network::get_state(float *v, float *a, float *ge, float *gi, int32_t *ref, int32_t *ring, int64_t *tick) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaStreamSynchronize(stream));
+  check_resident();
   const size_t N = size_t(n_);
   if (v) NGB_CUDA(cudaMemcpy(v, v_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
   if (a) NGB_CUDA(cudaMemcpy(a, a_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
@@ -836,6 +932,18 @@ void Network::enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_count
   if (ticks < 0) throw std::invalid_argument("ticks must be non-negative");
   const size_t words = (size_t(n_pre_) + 31) / 32;
   if (d_counts) NGB_CUDA(cudaMemsetAsync(d_counts, 0, size_t(ticks) * 16, st));
+  if (resident_) {
+    for (int k = 0; k < ticks;) {
+      const int chunk = std::min(ticks - k, kResidentChunk);
+      NGB_CUDA(cudaMemsetAsync(res_sync_.as<void>(), 0, 16, st));
+      cuda_check(launch_net_resident(dev_, res_, tick_ + k, chunk, d_spikes ? d_spikes + size_t(k) * words : nullptr,
+                                     d_counts ? d_counts + 2 * size_t(k) : nullptr, int(words), st),
+                 "resident tick launch");
+      k += chunk;
+    }
+    tick_ += ticks;
+    return;
+  }
   int k = 0;
   auto direct = [&](int kk) {
     const long long t = tick_ + kk;
@@ -871,6 +979,7 @@ void Network::run_host(int ticks, uint32_t *spikes, int64_t *counts) {
       NGB_CUDA(cudaMemcpyAsync(counts + 2 * size_t(done), rec_counts_.as<void>(), size_t(k) * 16,
                                cudaMemcpyDeviceToHost, stream));
     NGB_CUDA(cudaStreamSynchronize(stream));
+    check_resident();
   }
   NGB_CUDA(cudaStreamSynchronize(stream));
 }

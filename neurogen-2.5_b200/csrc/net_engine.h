@@ -82,6 +82,8 @@ public:
   void run_host(int ticks, uint32_t *spikes, int64_t *counts);
   void stats(int64_t *totals);
   bool split() const { return split_; }
+  bool resident() const { return resident_; }
+  const ResidentDev &resident_plan() const { return res_; }
 
   ng_net_config cfg;
   int device = 0;
@@ -108,6 +110,14 @@ private:
                        cudaStream_t st);
   void launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned long long *counts_row, cudaStream_t st);
   void capture_graph();
+  // Resident launch: plan, owner blocks, buffers.
+  bool resident_ = false;
+  ResidentDev res_{};
+  DeviceBuffer res_blocks_, res_lists_, res_sync_, res_err_;
+  static constexpr int kResidentChunk = 2048; // ticks per persistent launch
+  bool plan_resident(const HostCSR &h, bool required);
+  void build_owner_blocks();
+  void check_resident();
 };
 
 } // namespace ngb

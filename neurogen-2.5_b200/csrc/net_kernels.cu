@@ -20,15 +20,8 @@
 // Spike and event counts accumulate into one counter pair per 256-neuron
 // group, so the hot path has no same-address atomics.
 //
-// Numerics contract (shared with the C oracle, oracle/net_oracle.c): fp32
-// state, every operation rounded as written (__f*_rn intrinsics, -fmad=false),
-// exp() by the Cody-Waite + degree-7 Taylor scheme below, and the ring holding
-// integer multiples of 2^-24 nS so that concurrent deliveries sum exactly,
-// independent of order.  Results are bit-identical to the oracle.
-#include "net_kernels.h"
-
-#include <cuda_fp16.h>
-#include <cuda_runtime.h>
+// The neuron arithmetic and its numerics contract are in net_device.cuh.
+#include "net_device.cuh"
 
 namespace ngb {
 namespace {
@@ -36,76 +29,24 @@ namespace {
 constexpr int TB = 256; // threads per block (8 warps)
 constexpr int WARPS = TB / 32;
 
-__device__ __forceinline__ long long tick_of(const TickRef &r) { return r.t_dev ? *r.t_dev + r.k : r.k; }
+using namespace netdev;
 
-__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
-  z += 0x9E3779B97F4A7C15ull;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ bool drive_event(const NetDev &d, long long t, int i) {
-  const unsigned long long key = ((unsigned long long)t << 32) | (unsigned)i;
-  return (unsigned)(mix64(key ^ d.drive_key) >> 32) < d.drive_thr;
-}
-
-// exp(x), x <= 0: Cody-Waite reduction x = k ln2 + r (15-bit head of ln2 so
-// k*head is exact), e^r by its degree-7 Taylor polynomial, scale by 2^k.
-__device__ __forceinline__ float ng_expf(float x) {
-  if (x < -87.f) return 0.f;
-  const float kf = rintf(__fmul_rn(x, 1.44269504f));
-  const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(kf, 0.693145751953125f)), __fmul_rn(kf, 1.42860682e-06f));
-  float p = 0.000198412701f;
-  p = __fadd_rn(__fmul_rn(p, r), 0.00138888892f);
-  p = __fadd_rn(__fmul_rn(p, r), 0.00833333377f);
-  p = __fadd_rn(__fmul_rn(p, r), 0.0416666679f);
-  p = __fadd_rn(__fmul_rn(p, r), 0.166666672f);
-  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
-  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-  const int k = (int)kf;
-  if (k >= -126) return __fmul_rn(p, __int_as_float((127 + k) << 23));
-  return __fmul_rn(__fmul_rn(p, __int_as_float((127 + k + 64) << 23)), 5.42101086e-20f);
-}
-
-// Membrane, conductance, adaptation and refractory update of neuron i at tick
-// t (operation order of the oracle's on_run).  Returns the spike.
+// Membrane update of held neuron i at tick t: reads and clears its ring slot.
 __device__ __forceinline__ bool alif_update(const NetDev &d, long long t, int i) {
   const int slot = (int)(t & (kRingSlots - 1));
   int2 *rp = d.ring + (size_t)slot * d.n + i;
   const int2 r = *rp;
   *rp = make_int2(0, 0);
-  const int gidx = d.base + i; // global neuron index: E/I split and drive draw
-  const bool exc = gidx < d.n_exc;
-  float ge = __fadd_rn(__fmul_rn(d.ge[i], d.dE), __fmul_rn(__int2float_rn(r.x), kRingQuantum));
-  const float gi = __fadd_rn(__fmul_rn(d.gi[i], d.dI), __fmul_rn(__int2float_rn(r.y), kRingQuantum));
-  const bool ev = drive_event(d, t, gidx);
-  if (d.drive_kind == 0 && ev) ge = __fadd_rn(ge, d.drive_ns);
-  float a = __fmul_rn(d.a[i], d.dA);
-  const float g = __fadd_rn(__fadd_rn(d.g_leak, ge), gi);
-  const float vinf = __fdiv_rn(__fadd_rn(__fsub_rn(__fadd_rn(d.gLEL, __fmul_rn(d.e_inh, gi)), a), d.bias), g);
-  const int ref = d.ref[i];
-  const bool avail = ref <= 0;
-  const float cap = exc ? d.cap_e : d.cap_i;
-  const float decay = ng_expf(__fdiv_rn(__fmul_rn(d.neg_dt, g), cap));
-  float v = __fadd_rn(vinf, __fmul_rn(__fsub_rn(d.v[i], vinf), decay));
-  if (!avail) v = d.v_reset;
-  const bool s = d.drive_kind == 1 ? ev : (avail && v >= d.v_th);
-  if (s) v = d.v_reset;
-  int ref_next = ref > 0 ? ref - 1 : 0;
-  if (s) ref_next = d.ref_ticks;
-  if (s && exc) a = __fadd_rn(a, d.adapt_inc);
+  float v = d.v[i], a = d.a[i], ge = d.ge[i], gi = d.gi[i];
+  int ref = d.ref[i];
+  const bool s = alif_math(d, t, d.base + i, r, v, a, ge, gi, ref);
   d.v[i] = v;
   d.a[i] = a;
   d.ge[i] = ge;
   d.gi[i] = gi;
-  d.ref[i] = ref_next;
+  d.ref[i] = ref;
   return s;
 }
-
-// Fixed-point amount (2^-24 nS units) of a signed weight.
-__device__ __forceinline__ int quantum(float w) { return __float2int_rn(__fmul_rn(fabsf(w), 16777216.f)); }
 
 __device__ __forceinline__ int deliver(const NetDev &d, long long t, uint32_t word, float w) {
   if (w == 0.f) return 0;
@@ -114,10 +55,6 @@ __device__ __forceinline__ int deliver(const NetDev &d, long long t, uint32_t wo
   const int slot = (int)((t + dly) & (kRingSlots - 1));
   atomicAdd(reinterpret_cast<int *>(d.ring) + ((size_t)slot * d.n + post) * 2 + (w < 0.f ? 1 : 0), quantum(w));
   return 1;
-}
-
-__device__ __forceinline__ float half_bits(uint32_t bits16) {
-  return __half2float(__ushort_as_half((unsigned short)bits16));
 }
 
 // Push all outgoing CSR synapses of `pre` with the whole warp: each lane takes

@@ -71,4 +71,33 @@ constexpr int kNetBlock = 256; // neurons per membrane CTA
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s);
 void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s);
 
+// Resident launch shape (net_resident.cu): a persistent cooperative launch
+// runs many ticks with CTA c owning neurons [c*per_cta, (c+1)*per_cta), their
+// state and a ring of ring_depth slots in shared memory.
+constexpr int kResidentThreads = 1024;
+constexpr int kOwnerBlockSlots = 8; // event words per owner block
+struct ResidentDev {
+  int ctas;           // C (all co-resident)
+  int per_cta;        // P, a multiple of 32, at most 2048
+  int ring_depth;     // Dr: power of two >= the largest delay; 2*(Dr+1)*P < 2^16
+  int ev64;           // 1: 64-bit events (fp32 weights), 0: 32-bit (fp16)
+  const void *blocks; // [n_pre][C] owner blocks of 8 events, then overflow blocks
+  int *lists;         // [2][n_pre] spike ids of the tick, by tick parity
+  unsigned *sync;     // [0] grid barrier counter, [1 + t%3] list length of tick t;
+                      // zeroed before each launch
+  int *err;           // set to 1 by a barrier timeout
+};
+size_t resident_smem_bytes(const ResidentDev &r);
+// Co-resident CTAs of the resident kernel at this shared-memory size (0: none).
+int resident_max_ctas(bool ev64, size_t smem);
+// ticks ticks from tick t0; spikes_out [ticks][words] and counts [ticks][2] optional.
+cudaError_t launch_net_resident(const NetDev &d, const ResidentDev &r, long long t0, int ticks, uint32_t *spikes_out,
+                                unsigned long long *counts, int words, cudaStream_t s);
+// Owner-block construction from the device CSR: overflow blocks needed
+// (added to *need), then the blocks themselves (array pre-filled with all-ones
+// words; overflow blocks taken from *cursor; *err = 2 past `capacity`).
+void launch_owner_count(const NetDev &d, const ResidentDev &r, unsigned long long *need, cudaStream_t s);
+void launch_owner_fill(const NetDev &d, const ResidentDev &r, void *blocks, unsigned long long *cursor,
+                       unsigned long long capacity, int *err, cudaStream_t s);
+
 } // namespace ngb

@@ -28,7 +28,7 @@ EXPORTS = (
     'ng_net_default_config', 'ng_net_create', 'ng_net_create_edges', 'ng_net_destroy',
     'ng_net_synapses', 'ng_net_export', 'ng_net_set_state', 'ng_net_get_state', 'ng_net_run',
     'ng_net_run_device', 'ng_topology_create', 'ng_topology_destroy', 'ng_topology_synapses',
-    'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static',
+    'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static', 'ng_net_launch_kind',
     'ng_net_create_partitioned', 'ng_nccl_unique_id',
 )
 
@@ -117,6 +117,8 @@ def library():
     lib.ng_net_destroy.restype = None
     lib.ng_net_synapses.argtypes = [vp]
     lib.ng_net_synapses.restype = ct.c_int64
+    lib.ng_net_launch_kind.argtypes = [vp]
+    lib.ng_net_launch_kind.restype = ct.c_int
     lib.ng_net_export.argtypes = [vp, I32, I32, I32, F32]
     lib.ng_net_export.restype = ci
     lib.ng_net_set_state.argtypes = [vp, vp, vp, vp, vp, vp, vp, ct.c_int64]

@@ -31,7 +31,7 @@ def default_config(**overrides):
         elif key == 'storage' and isinstance(value, str):
             value = {'csr': 0, 'bsr': 1}[value]
         elif key == 'launch' and isinstance(value, str):
-            value = {'auto': 0, 'fused': 1, 'split': 2}[value]
+            value = {'auto': 0, 'fused': 1, 'split': 2, 'resident': 3}[value]
         if not hasattr(cfg, key):
             raise KeyError(key)
         setattr(cfg, key, value)
@@ -126,6 +126,11 @@ class Network:
     @property
     def synapses(self):
         return self.lib.ng_net_synapses(self.h)
+
+    @property
+    def launch(self):
+        """Launch shape in use: 'fused', 'split' or 'resident'."""
+        return {1: 'fused', 2: 'split', 3: 'resident'}[self.lib.ng_net_launch_kind(self.h)]
 
     def export(self):
         m = self.synapses

@@ -1,6 +1,6 @@
 """GPU parity of the language core against the reference's own native CPU library.
 
-Bars (north star): spike indices identical for the first 100 ticks; state within 1e-5
+Bars: spike indices identical for the first 100 ticks; state within 1e-5
 relative; logits within 1e-4 relative.  The engine reproduces the reference's fp32 operation
 order, so most outputs are bit-identical; the measured counts are printed for the record.
 """

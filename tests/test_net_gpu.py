@@ -15,6 +15,9 @@ from oracle.net import NetOracle, unpack_spikes
 
 pytestmark = pytest.mark.gpu
 
+LAUNCH = {'fused': 1, 'split': 2, 'resident': 3}
+LAUNCHES = list(LAUNCH)
+
 
 def run_both(cfg, ticks, state=None):
     topo = Topology(cfg)
@@ -36,10 +39,10 @@ def assert_same_state(net, orc):
     assert a['tick'] == b['tick']
 
 
-@pytest.mark.parametrize('launch', ['fused', 'split'])
+@pytest.mark.parametrize('launch', LAUNCHES)
 def test_isolated_8k_bit_exact_200_ticks(launch):
     cfg = isolated_8k()
-    cfg.launch = {'fused': 1, 'split': 2}[launch]
+    cfg.launch = LAUNCH[launch]
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 200)
     assert oc[:, 0].sum() > 1000
     np.testing.assert_array_equal(gs, os_)  # every spike of every tick
@@ -47,8 +50,8 @@ def test_isolated_8k_bit_exact_200_ticks(launch):
     assert_same_state(net, orc)
 
 
-@pytest.mark.parametrize('launch', ['fused', 'split'])
-@pytest.mark.parametrize('storage', ['csr', 'bsr'])
+@pytest.mark.parametrize('storage,launch', [('csr', 'fused'), ('csr', 'split'), ('csr', 'resident'),
+                                            ('bsr', 'fused'), ('bsr', 'split')])
 def test_block_matrix_both_storages_bit_exact(storage, launch):
     cfg = default_config(n=4096, n_exc=3277, topology='bsr16', bsr_blocks=32, bsr_fill=64,
                          weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, storage=storage,
@@ -59,7 +62,7 @@ def test_block_matrix_both_storages_bit_exact(storage, launch):
     assert_same_state(net, orc)
 
 
-@pytest.mark.parametrize('launch', ['fused', 'split'])
+@pytest.mark.parametrize('launch', LAUNCHES)
 def test_fixed_fanin_fp16_imposed_bit_exact(launch):
     cfg = default_config(n=16384, n_exc=13107, topology='fixed_fanin', fanin=128, weight_kind='halfnormal_f16',
                          w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8, launch=launch)
@@ -69,7 +72,7 @@ def test_fixed_fanin_fp16_imposed_bit_exact(launch):
     assert_same_state(net, orc)
 
 
-@pytest.mark.parametrize('launch', ['fused', 'split'])
+@pytest.mark.parametrize('launch', LAUNCHES)
 def test_ragged_sizes_and_empty_network(launch):
     # n not a multiple of 32 (partial last warp) and an empty synapse set.
     cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3, launch=launch)
@@ -148,13 +151,13 @@ def test_scaled_262k_csr_properties():
     assert net.get_state()['ring'].astype(np.int64).sum() == pending
 
 
-@pytest.mark.parametrize('launch', ['fused', 'split'])
+@pytest.mark.parametrize('launch', LAUNCHES)
 def test_graph_replay_equals_recorded_run(launch):
     """The graph path (no per-tick outputs, device tick counter) and the recorded path give the
     same state, totals and trajectory, including a run length that is not a multiple of the
     graph length and a resume from an arbitrary tick."""
     cfg = isolated_8k(seed=5)
-    cfg.launch = {'fused': 1, 'split': 2}[launch]
+    cfg.launch = LAUNCH[launch]
     topo = Topology(cfg)
     a, b = topo.network(), topo.network()
     _, ca = a.run(150)
@@ -181,8 +184,10 @@ def test_pipelined_graph_full_size():
     tick) ends in the same state and totals as the recorded path, which runs every push whole and
     in order on one stream."""
     cfg = scaled_262k('csr', rate=0.05)
+    cfg.launch = LAUNCH['split']
     topo = Topology(cfg)
     a, b = topo.network(), topo.network()
+    assert a.launch == 'split'
     _, ca = a.run(3 + 1 + 2 * 64)
     b.run_device(3)
     b.run_device(1 + 2 * 64)  # from tick 3: one direct tick, then two graph replays
@@ -190,3 +195,33 @@ def test_pipelined_graph_full_size():
     for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
         assert np.array_equal(sa[k], sb[k]), k
     assert b.stats() == (int(ca[:, 0].sum()), int(ca[:, 1].sum()))
+
+
+def test_resident_full_size_equals_split():
+    """N=262,144 fixed fan-in at 5%: the resident launch (state and ring in shared memory, owner
+    blocks with overflow chains) gives every spike, count and state bit of the split launch, across
+    launch boundaries (2,048 ticks a launch) and a resume from an odd tick."""
+    cfg = scaled_262k('csr', rate=0.05)
+    topo = Topology(cfg)
+    cfg_split = scaled_262k('csr', rate=0.05)
+    cfg_split.launch = LAUNCH['split']
+    res, ref = topo.network(), Topology(cfg_split).network()
+    assert res.launch == 'resident' and ref.launch == 'split'
+    gs, gc = res.run(37)
+    rs, rc = ref.run(37)
+    np.testing.assert_array_equal(gs, rs)
+    np.testing.assert_array_equal(gc, rc)
+    res.run_device(2100)
+    ref.run_device(2100)
+    sa, sb = res.get_state(), ref.get_state()
+    for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
+        assert np.array_equal(sa[k], sb[k]), k
+    assert sa['tick'] == sb['tick'] == 2137
+    assert res.stats() == ref.stats()
+
+
+def test_auto_launch_choice():
+    assert Topology(isolated_8k()).network().launch == 'resident'
+    assert Topology(scaled_262k('bsr', rate=0.03)).network().launch == 'split'
+    small = default_config(n=1000, launch='split')
+    assert Topology(small).network().launch == 'split'
