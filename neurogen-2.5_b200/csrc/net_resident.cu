@@ -86,27 +86,25 @@ struct Ev64 {
   __device__ static int amount(word e) { return (int)(uint32_t)e; }
 };
 
-// One owner block (8 words) with 16-byte loads, streamed past L1.
+// One owner block (8 words, 32-byte aligned) with 256-bit loads that take no
+// L1 line: every lane of a warp reads a different row, so L1 would only cost
+// tag work and line allocations for data that is used once.
+__device__ __forceinline__ void ld_block256(const void *p, uint32_t (&v)[8]) {
+  asm volatile("ld.global.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "l"(p));
+}
+
 template <class E> __device__ __forceinline__ void load_block(const typename E::word *p, typename E::word (&w)[kSlots]) {
-  constexpr int kVec = (int)(sizeof(typename E::word) * kSlots / 16);
-  const uint4 *q = reinterpret_cast<const uint4 *>(p);
-  uint4 v[kVec];
-#pragma unroll
-  for (int k = 0; k < kVec; ++k) v[k] = __ldcs(q + k);
   if constexpr (sizeof(typename E::word) == 4) {
-#pragma unroll
-    for (int k = 0; k < kVec; ++k) {
-      w[4 * k] = v[k].x;
-      w[4 * k + 1] = v[k].y;
-      w[4 * k + 2] = v[k].z;
-      w[4 * k + 3] = v[k].w;
-    }
+    ld_block256(p, w);
   } else {
+    uint32_t v[2][8];
+    ld_block256(p, v[0]);
+    ld_block256(reinterpret_cast<const uint32_t *>(p) + 8, v[1]);
 #pragma unroll
-    for (int k = 0; k < kVec; ++k) {
-      w[2 * k] = (unsigned long long)v[k].x | ((unsigned long long)v[k].y << 32);
-      w[2 * k + 1] = (unsigned long long)v[k].z | ((unsigned long long)v[k].w << 32);
-    }
+    for (int k = 0; k < kSlots; ++k)
+      w[k] = (unsigned long long)v[k >> 2][2 * (k & 3)] | ((unsigned long long)v[k >> 2][2 * (k & 3) + 1] << 32);
   }
 }
 
