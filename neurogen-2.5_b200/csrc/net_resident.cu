@@ -22,8 +22,8 @@
 //   4. each warp takes rounds of 32 list entries: each lane loads the owner
 //      block (p, c) of one spike (the next two rounds' blocks stay in flight
 //      while it delivers one) and delivers its 8 slots with predicated
-//      shared-memory atomics.  Overflow links go to a shared queue and are
-//      delivered the same way once the rounds are done.
+//      shared-memory atomics.  A warp delivers the overflow blocks it met
+//      right after its own rounds (deeper links: one CTA-wide pass).
 // Deliveries never leave the owning CTA, so the tick needs no scattered
 // global atomics; the only global traffic is the owner blocks of the spiking
 // rows, the spike list and the barrier.  The shared ring holds exactly the
@@ -46,7 +46,8 @@ constexpr int RT = kResidentThreads;
 constexpr int RW = RT / 32;
 constexpr int kSlots = kOwnerBlockSlots;
 constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull; // 2 s
-constexpr int kLinkCap = 512; // queued overflow links per pass
+constexpr int kLinkCap = 512;  // queued overflow links per CTA-wide pass
+constexpr int kWarpLinks = 32; // overflow links a warp queues for itself per tick
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -193,9 +194,8 @@ __device__ __forceinline__ int deliver_lane(const RingAt &ra, const typename E::
 // arrived) into count_s.
 __device__ __forceinline__ bool grid_sync(const ResidentDev &r, unsigned target, const unsigned *count, int &ok_s,
                                           int &count_s) {
-  __syncthreads(); // the CTA's writes happen before thread 0's fence and release
+  __syncthreads(); // the CTA's writes happen before thread 0's (cumulative) release
   if (threadIdx.x == 0) {
-    __threadfence();
     red_release_add_u32(r.sync, 1u);
     int ok = 1;
     const unsigned long long start = global_ns();
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
   using W = typename E::word;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ unsigned long long red_s[RW];
-  __shared__ int ok_s, spikes_s, link_n_s[2];
+  __shared__ int ok_s, spikes_s, link_n_s[2], warp_n_s[RW];
   const int C = r.ctas, P = r.per_cta, Dr = r.ring_depth, dr_mask = Dr - 1;
   const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gbase = c * P;
@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
   int *ref_s = reinterpret_cast<int *>(gi_s + P);
   uint32_t *word_s = reinterpret_cast<uint32_t *>(ref_s + P); // [P/32], P <= 2048
   int *link_q = reinterpret_cast<int *>(word_s + P / 32);      // [2][kLinkCap]
+  int *warp_q = link_q + 2 * kLinkCap;                          // [RW][kWarpLinks]
   const W *blocks = static_cast<const W *>(r.blocks);
 
   for (int i = tid; i < Pc; i += RT) {
@@ -262,6 +263,7 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
   }
   for (int i = tid; i < Dr * 2 * P; i += RT) ring_s[i] = 0;
   if (tid == 0) link_n_s[0] = link_n_s[1] = 0;
+  if (lane == 0) warp_n_s[warp] = 0;
   __syncthreads();
 
   unsigned long long events = 0, spikes = 0;
@@ -331,6 +333,7 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
     const int *lst = r.lists + (size_t)par * d.n_pre;
     const RingAt ra{ring_s, (uint32_t)(2 * P * (int)(t & dr_mask)), (uint32_t)(2 * P * Dr)};
     const LinkQueue links0{link_q, &link_n_s[0], kLinkCap};
+    const LinkQueue own_links{warp_q + warp * kWarpLinks, &warp_n_s[warp], kWarpLinks};
     constexpr int D = E::kDepth;
     // This warp's rounds are warp + m*RW, m < M; the blocks of rounds m+1..m+D
     // are in flight while round m is delivered (buffers renamed statically).
@@ -363,9 +366,27 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
         if (m + ph < M) {
           fetch(pn, b[(ph + D) % (D + 1)]); // round m + ph + D
           pn = list_at(m + ph + D + 1);
-          tick_events += (unsigned long long)deliver_lane<E>(ra, blocks, b[ph], links0);
+          tick_events += (unsigned long long)deliver_lane<E>(ra, blocks, b[ph], own_links);
         }
       }
+    }
+    // The overflow blocks this warp met, delivered by the warp itself while the
+    // others may still be in their rounds; their own links go to the CTA queue.
+    __syncwarp();
+    {
+      const int n = min(warp_n_s[warp], kWarpLinks);
+      if (n > 0) {
+        W w[kSlots];
+        if (lane < n) {
+          load_block<E>(blocks + (size_t)own_links.q[lane] * kSlots, w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSlots; ++j) w[j] = E::kEmpty;
+        }
+        tick_events += (unsigned long long)deliver_lane<E>(ra, blocks, w, links0);
+      }
+      __syncwarp();
+      if (lane == 0) warp_n_s[warp] = 0;
     }
     __syncthreads();
     // Overflow blocks, in rounds of 32; their own links go to the other queue.
@@ -549,7 +570,8 @@ template <class E> void *resident_kernel() { return reinterpret_cast<void *>(&k_
 
 size_t resident_smem_bytes(const ResidentDev &r) {
   const size_t P = size_t(r.per_cta);
-  return size_t(r.ring_depth) * P * 8 + P * 20 + (P / 32) * 4 + 2 * size_t(kLinkCap) * 4;
+  return size_t(r.ring_depth) * P * 8 + P * 20 + (P / 32) * 4 + 2 * size_t(kLinkCap) * 4 +
+         size_t(RW) * kWarpLinks * 4;
 }
 
 int resident_max_ctas(bool ev64, size_t smem) {
