@@ -196,6 +196,20 @@ def tick_bytes(cfg, spikes, events, held=None):
     return per_neuron + events * (4 + wbytes + 1)
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per tick from one ncu capture of the
+# dominant kernel on this workload (profiles/k_net_resident_scaled_tick_262144_csr.md: 64 ticks at a
+# 3% spike rate).  Owner-block traffic is proportional to the spikes, so it is scaled by the run's rate.
+NCU_TRAFFIC = {('scaled_tick_262144_csr', 'resident'): (2.400492e9 + 4.731392e6, 64, 0.030017)}
+
+
+def tick_traffic(workload, mode, rate):
+    entry = NCU_TRAFFIC.get((workload, mode))
+    if not entry:
+        return None
+    total, ticks, rate0 = entry
+    return total / ticks * rate / rate0
+
+
 KERNEL_OF_LAUNCH = {'fused': 'k_net_fused', 'split': 'tick = k_net_alif + k_net_push',
                     'resident': 'k_net_resident (persistent, 2,048 ticks a launch)'}
 
@@ -276,7 +290,9 @@ def bench_ticks(args, dist):
                    'launch': mode, 'setup_s': round(setup_s, 2)},
         'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
-                     'frac': achieved / peak_total, 'traffic': None, 'bytes_per_tick': b_tick,
+                     'frac': achieved / peak_total,
+                     'traffic': tick_traffic(wl, mode, spikes / total_ticks / cfg.n) if not part else None,
+                     'traffic_unit': 'bytes/tick (ncu, scaled by spike rate)', 'bytes_per_tick': b_tick,
                      'kernel': KERNEL_OF_LAUNCH[mode], 'peak_source': src},
         'gpu_launches': tick_launches(mode, ticks) * args.steps,
         'clocks': clk.summary(),
@@ -503,6 +519,13 @@ def reference_arm(args):
             orc.run_mt(sample)
         el = time.time() - t0
         value, unit = sample * args.steps / el / scale, 'ticks/s'
+        ms_per_step = el / args.steps * 1e3 * scale
+        config = {'workload': wl, 'n': cfg.n * scale, 'ticks_per_step': sample,
+                  'fanin': cfg.fanin if cfg.topology == 1 else None,
+                  'bsr': [cfg.bsr_blocks, cfg.bsr_fill] if cfg.topology == 2 else None,
+                  'spike_rate': args.rate if cfg.drive_kind == 1 else None,
+                  'weights': 'fp16' if cfg.weight_kind else 'fp32', 'delays': [cfg.delay_min, cfg.delay_max]}
+        scaling = 'strong' if args.workload == 'partitioned4m' else 'weak'
         kind, desc = 'port', f'{sample} ticks per step of {wl} (oracle/net_oracle.c, OpenMP)'
         if scale > 1:
             desc += f'; 1/{scale}-scale network (N={cfg.n:,}), time per tick x{scale}'
@@ -531,12 +554,16 @@ def reference_arm(args):
                 list(pool.map(work, range(threads)))
             el = time.time() - t0
         value, unit = threads * per_step * args.steps / el, 'tokens/s'
+        ms_per_step = el / args.steps * 1e3
+        config = {'workload': wl, 'sessions': 1 if args.workload == 'bc250' else SESSIONS,
+                  'tokens_per_step': per_step * threads}
+        scaling = 'weak' if args.workload == 'bc250' else 'strong'
         kind = 'reference'
         desc = f'{per_step} tokens per step on each of {threads} independent sessions (one engine per thread)'
         metric = METRIC_TOKENS
-    return {'metric': metric, 'value': value, 'unit': unit, 'n_gpus': 0, 'steps': args.steps,
-            'warmup': args.warmup, 'higher_is_better': True, 'impl': 'reference', 'dtype': 'fp32',
-            'data': 'synthetic', 'config': {'workload': wl},
+    return {'metric': metric, 'value': value, 'unit': unit, 'n_gpus': int(os.environ.get('WORLD_SIZE', '1')),
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': scaling, 'impl': 'reference', 'dtype': 'fp32', 'data': 'synthetic', 'config': config,
             'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores if kind == 'port' or threads > 1 else 1,
                              'kind': kind, 'sample': desc},
             'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
