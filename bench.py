@@ -277,7 +277,8 @@ def bench_ticks(args, dist):
     line = {
         'metric': METRIC_TICKS, 'value': total_ticks * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
         'n_gpus': dist.world, 'steps': args.steps, 'warmup': args.warmup,
-        'ms_per_step': t_max / args.steps * 1e3, 'higher_is_better': True, 'scaling': 'weak',
+        'ms_per_step': t_max / args.steps * 1e3, 'higher_is_better': True,
+        'scaling': 'strong' if part else 'weak',
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic',
         'config': {'workload': wl, 'n': cfg.n, 'ticks_per_step': ticks,
                    'fanin': cfg.fanin if cfg.topology == 1 else None,

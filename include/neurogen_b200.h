@@ -179,7 +179,10 @@ typedef struct {
 void ng_net_default_config(ng_net_config *cfg);
 
 /* Generate the network described by `cfg` (deterministic in cfg->seed) and
- * upload it to the current CUDA device.  Returns NULL on error. */
+ * upload it to the current CUDA device.  Fixed fan-in networks with fp16
+ * weights in CSR storage are drawn on the device (same draws as
+ * ng_topology_create; the order of synapses inside a row may differ, spikes
+ * and state do not).  Returns NULL on error. */
 void *ng_net_create(const ng_net_config *cfg);
 
 /* Build a network from caller arrays instead of generating one: synapse list

@@ -56,6 +56,9 @@ void *ng_net_create(const ng_net_config *cfg) {
   return guarded_ptr([&]() -> void * {
     if (!cfg) throw std::invalid_argument("Null network config");
     if (cfg->part_world > 1) throw std::invalid_argument("Use ng_net_create_partitioned for part_world > 1");
+    // Fixed fan-in fp16 networks in CSR storage draw their synapses on the device.
+    if (cfg->topology == NG_TOPO_FIXED_FANIN && cfg->weight_kind == NG_W_HALFNORMAL_F16 && cfg->storage == 0)
+      return new Network(*cfg, nullptr, DeviceFanin{});
     std::unique_ptr<Topology> t(make_topology(*cfg));
     return new Network(*t);
   });
@@ -82,6 +85,9 @@ void *ng_net_create_partitioned(const ng_net_config *cfg, const void *nccl_id) {
     if (!cfg) throw std::invalid_argument("Null network config");
     if (cfg->part_world < 2) throw std::invalid_argument("ng_net_create_partitioned needs part_world >= 2");
     if (!nccl_id) throw std::invalid_argument("Null NCCL unique id");
+    // Fixed fan-in fp16 networks (the large ones) draw their synapses on the device.
+    if (cfg->topology == NG_TOPO_FIXED_FANIN && cfg->weight_kind == NG_W_HALFNORMAL_F16)
+      return new Network(*cfg, nccl_id, DeviceFanin{});
     std::unique_ptr<Topology> t(make_topology(*cfg));
     return new Network(*t, nccl_id);
   });

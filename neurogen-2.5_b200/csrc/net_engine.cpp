@@ -602,6 +602,99 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
     d.mid = mid_.as<int>();
     for (int x : csr->outdeg) nnz_ += x;
   }
+  int max_delay = 1;
+  if (csr)
+    for (uint32_t w : csr->syn) max_delay = std::max(max_delay, int(w >> 28) + 1);
+  init_state(nccl_id, csr != nullptr, max_delay);
+}
+
+// Partitioned fixed fan-in network whose synapses are drawn on the device:
+// the rank holds posts [lo, hi) and the rows of every presynaptic cell onto them.
+Network::Network(const ng_net_config &c, const void *nccl_id, DeviceFanin) : cfg(c) {
+  validate_config(c);
+  if (c.topology != NG_TOPO_FIXED_FANIN || c.storage != 0 || c.weight_kind != NG_W_HALFNORMAL_F16)
+    throw std::invalid_argument("Device generation covers fixed fan-in CSR networks with fp16 weights");
+  device = require_sm100_device();
+  int lo = 0, hi = 0;
+  partition_range(c, lo, hi);
+  n_pre_ = c.n;
+  n_ = hi - lo;
+  base_ = lo;
+  world_ = c.part_world > 1 ? c.part_world : 1;
+  rank_ = world_ > 1 ? c.part_rank : 0;
+  NetDev &d = dev_;
+  d.n = n_;
+  d.n_exc = c.n_exc;
+  d.n_pre = n_pre_;
+  d.base = base_;
+  generate_fanin_device(lo, hi);
+  init_state(nccl_id, true, c.delay_max);
+}
+
+void Network::generate_fanin_device(int lo, int hi) {
+  const ng_net_config &c = cfg;
+  const int n = c.n;
+  FaninGen g{};
+  g.n = n;
+  g.n_exc = c.n_exc;
+  g.lo = lo;
+  g.np = hi - lo;
+  g.fanin = c.fanin;
+  g.delay_min = c.delay_min;
+  g.delay_span = c.delay_max - c.delay_min + 1;
+  g.sigma = c.w_sigma;
+  g.key_pre = Stream(c.seed, S_PRE).key;
+  g.key_delay = Stream(c.seed, S_DELAY).key;
+  g.key_w1 = Stream(c.seed, S_W1).key;
+  g.key_w2 = Stream(c.seed, S_W2).key;
+  // Pass 1: synapses per row, delay-1 apart -> padded row layout on the host.
+  DeviceBuffer c12(size_t(n) * 8 + 4);
+  int *c1 = c12.as<int>(), *c2 = c1 + n, *bad = c2 + n;
+  NGB_CUDA(cudaMemset(c1, 0, size_t(n) * 8));
+  NGB_CUDA(cudaMemset(bad, 0x7F, 4));
+  launch_fanin_count(g, c1, c2, nullptr);
+  NGB_CUDA(cudaGetLastError());
+  std::vector<int> h1(n), h2(n), mid(n), outdeg(n);
+  NGB_CUDA(cudaMemcpy(h1.data(), c1, size_t(n) * 4, cudaMemcpyDeviceToHost));
+  NGB_CUDA(cudaMemcpy(h2.data(), c2, size_t(n) * 4, cudaMemcpyDeviceToHost));
+  std::vector<long long> row(size_t(n) + 1, 0);
+  for (int i = 0; i < n; ++i) {
+    mid[i] = int(pad8(h1[i]));
+    outdeg[i] = h1[i] + h2[i];
+    nnz_ += outdeg[i];
+    row[i + 1] = row[i] + pad8(h1[i]) + pad8(h2[i]);
+  }
+  const size_t total = size_t(row[n]) + kTailPad;
+  row_ = upload_vec(row);
+  mid_ = upload_vec(mid);
+  outdeg_ = upload_vec(outdeg);
+  syn_.reset(total * 4);
+  w_.reset(total * 2);
+  NGB_CUDA(cudaMemset(syn_.as<void>(), 0, total * 4)); // padding: post 0, delay 1, weight 0
+  NGB_CUDA(cudaMemset(w_.as<void>(), 0, total * 2));
+  // Pass 2: place the synapses (the counters become cursors).
+  NGB_CUDA(cudaMemset(c1, 0, size_t(n) * 8));
+  launch_fanin_fill(g, row_.as<long long>(), mid_.as<int>(), c1, c2, syn_.as<uint32_t>(), w_.as<uint16_t>(), bad,
+                    nullptr);
+  NGB_CUDA(cudaGetLastError());
+  int bad_post = 0;
+  NGB_CUDA(cudaMemcpy(&bad_post, bad, 4, cudaMemcpyDeviceToHost));
+  if (bad_post != 0x7F7F7F7F)
+    throw std::invalid_argument("Synaptic input of neuron " + std::to_string(bad_post) +
+                                " can exceed the delay ring's fixed-point range (127 nS per slot)");
+  NetDev &d = dev_;
+  d.row = row_.as<long long>();
+  d.syn = syn_.as<uint32_t>();
+  d.w = w_.as<void>();
+  d.w_half = 1;
+  d.mid = mid_.as<int>();
+}
+
+// State, counters, launch shape and (partitioned) communicator; the synapses
+// are on the device already.
+void Network::init_state(const void *nccl_id, bool csr, int max_delay) {
+  const ng_net_config &c = cfg;
+  NetDev &d = dev_;
   d.outdeg = outdeg_.as<int>();
   const size_t N = size_t(n_);
   v_.reset(N * 4);
@@ -647,7 +740,7 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
   // the presynaptic groups); tick.
   // Resident launch (persistent kernel, state in shared memory) when asked
   // for, or by default when the network qualifies and fits.
-  if (csr && world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(*csr, c.launch == 3);
+  if (csr && world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(max_delay, c.launch == 3);
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
   const size_t groups = std::max({pre_groups, (N + kNetBlock - 1) / kNetBlock, size_t(resident_ ? res_.ctas : 0)});
   const size_t bm_words = pre_groups * (kNetBlock / 32);
@@ -678,7 +771,7 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
 // that small networks use few CTAs), one CTA per SM at most, shared memory for
 // the state, a ring of Dr slots and the warps' event staging.  Returns false
 // (or throws, when the resident launch was asked for) if it does not fit.
-bool Network::plan_resident(const HostCSR &h, bool required) {
+bool Network::plan_resident(int max_delay, bool required) {
   auto fail = [&](const std::string &why) -> bool {
     if (required) throw std::invalid_argument("Resident launch unavailable: " + why);
     return false;
@@ -688,8 +781,6 @@ bool Network::plan_resident(const HostCSR &h, bool required) {
   NGB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   NGB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
   if (!coop) return fail("the device has no cooperative launch");
-  int max_delay = 1;
-  for (uint32_t w : h.syn) max_delay = std::max(max_delay, int(w >> 28) + 1);
   int dr = 1;
   while (dr < max_delay) dr <<= 1;
   const bool ev64 = dev_.w_half == 0;

@@ -62,11 +62,14 @@ void csr_from_edges(const ng_net_config &c, int64_t nnz, const int32_t *pre, con
                     const int32_t *delay, const float *w, HostCSR &out);
 void validate_config(const ng_net_config &c);
 
+struct DeviceFanin {}; // tag: draw a fixed fan-in network's synapses on the device
+
 class Network {
 public:
   // nccl_id: 128-byte NCCL unique id, required when cfg.part_world > 1
   // (collective: every rank constructs its partition at the same time).
   explicit Network(const Topology &topo, const void *nccl_id = nullptr);
+  Network(const ng_net_config &cfg, const void *nccl_id, DeviceFanin);
   ~Network();
   Network(const Network &) = delete;
   Network &operator=(const Network &) = delete;
@@ -115,7 +118,9 @@ private:
   ResidentDev res_{};
   DeviceBuffer res_blocks_, res_lists_, res_sync_, res_err_;
   static constexpr int kResidentChunk = 2048; // ticks per persistent launch
-  bool plan_resident(const HostCSR &h, bool required);
+  bool plan_resident(int max_delay, bool required);
+  void generate_fanin_device(int lo, int hi);
+  void init_state(const void *nccl_id, bool csr, int max_delay);
   void build_owner_blocks();
   void check_resident();
 };

@@ -100,4 +100,19 @@ void launch_owner_count(const NetDev &d, const ResidentDev &r, unsigned long lon
 void launch_owner_fill(const NetDev &d, const ResidentDev &r, void *blocks, unsigned long long *cursor,
                        unsigned long long capacity, int *err, cudaStream_t s);
 
+// Fixed fan-in synapses drawn on the device for held posts [lo, lo + np) of an
+// n-neuron network (net_generate.cu), fp16 weights.  Keys are the host
+// generator's stream keys.
+struct FaninGen {
+  int n, n_exc, lo, np, fanin, delay_min, delay_span;
+  float sigma;
+  unsigned long long key_pre, key_delay, key_w1, key_w2;
+};
+// c1/c2[pre] += delay-1 / delay>=2 synapses of row pre.
+void launch_fanin_count(const FaninGen &g, int *c1, int *c2, cudaStream_t s);
+// Writes syn/w16 at row[pre] (+ mid[pre] for delay>=2) through the cursors;
+// *bad_post = lowest held post whose input can overflow the ring (else unchanged).
+void launch_fanin_fill(const FaninGen &g, const long long *row, const int *mid, int *cur1, int *cur2, uint32_t *syn,
+                       uint16_t *w16, int *bad_post, cudaStream_t s);
+
 } // namespace ngb

@@ -225,3 +225,36 @@ def test_auto_launch_choice():
     assert Topology(scaled_262k('bsr', rate=0.03)).network().launch == 'split'
     small = default_config(n=1000, launch='split')
     assert Topology(small).network().launch == 'split'
+
+
+def edges_sorted(edges):
+    pre, post, delay, w = edges
+    order = np.lexsort((w.view(np.uint32), delay, post, pre))
+    return pre[order], post[order], delay[order], w[order]
+
+
+def test_device_generated_fanin_equals_host_generated():
+    """ng_net_create draws fixed fan-in fp16 networks on the device: the same synapses as the host
+    generator (ng_topology_create) and, run side by side, every spike and state bit."""
+    cfg = default_config(n=16384, n_exc=13107, topology='fixed_fanin', fanin=128, weight_kind='halfnormal_f16',
+                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8)
+    dev, host = Network(cfg), Topology(cfg).network()
+    assert dev.synapses == host.synapses == 16384 * 128
+    for a, b in zip(edges_sorted(dev.export()), edges_sorted(host.export())):
+        assert np.array_equal(a, b)
+    ds, dc = dev.run(40)
+    hs, hc = host.run(40)
+    np.testing.assert_array_equal(ds, hs)
+    np.testing.assert_array_equal(dc, hc)
+    a, b = dev.get_state(), host.get_state()
+    for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
+        assert np.array_equal(a[k], b[k]), k
+
+
+def test_device_generation_checks_the_ring_range():
+    cfg = default_config(n=4096, n_exc=3276, topology='fixed_fanin', fanin=512, weight_kind='halfnormal_f16',
+                         w_mu=0.0, w_sigma=2.0, seed=3)
+    with pytest.raises(ValueError, match='fixed-point range'):
+        Topology(cfg)
+    with pytest.raises(ValueError, match='fixed-point range'):
+        Network(cfg)
