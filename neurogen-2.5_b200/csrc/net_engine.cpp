@@ -794,6 +794,9 @@ bool Network::plan_resident(int max_delay, bool required) {
   r.ctas = (n_ + P - 1) / P;
   r.ring_depth = dr;
   r.ev64 = ev64 ? 1 : 0;
+  // Failure-path tests: an unreachable first barrier, so every CTA's bounded
+  // wait runs out and the launch reports the error instead of running.
+  if (const char *env = std::getenv("NEUROGEN_TEST_RESIDENT_STALL")) r.stall_test = std::atoi(env) ? 1 : 0;
   if (!ev64 && 2 * (dr + 1) * P >= 65536) return fail("ring offsets of " + std::to_string(P) + " neurons do not fit 16 bits");
   const size_t smem = resident_smem_bytes(r);
   if (smem + 2048 > size_t(optin)) // static shared memory and slack

@@ -81,6 +81,7 @@ struct ResidentDev {
   int per_cta;        // P, a multiple of 32, at most 2048
   int ring_depth;     // Dr: power of two >= the largest delay; 2*(Dr+1)*P < 2^16
   int ev64;           // 1: 64-bit events (fp32 weights), 0: 32-bit (fp16)
+  int stall_test;     // failure-path tests only: 1 makes the first barrier wait run out
   const void *blocks; // [n_pre][C] owner blocks of 8 events, then overflow blocks
   int *lists;         // [2][n_pre] spike ids of the tick, by tick parity
   unsigned *sync;     // [0] grid barrier counter, [1 + t%3] list length of tick t;

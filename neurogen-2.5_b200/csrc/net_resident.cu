@@ -325,7 +325,8 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
       }
     }
     // 3. Past the barrier every CTA's ids are in the list, and spikes_s holds their number.
-    if (!grid_sync(r, (unsigned)C * (unsigned)(k + 1), r.sync + 1 + mod3, ok_s, spikes_s)) return;
+    if (!grid_sync(r, (unsigned)C * (unsigned)(k + 1) + (unsigned)r.stall_test, r.sync + 1 + mod3, ok_s, spikes_s))
+      return;
     // Tick t-1's counter has been read by every CTA: clear it for tick t+2.
     if (c == 0 && tid == 0) r.sync[1 + (int)((t + 2) % 3)] = 0u;
     // 4. Deliver the owner blocks (p, c) of this tick's spikes.

@@ -347,3 +347,108 @@ class NativeLanguageModel:
 
 def config_dict(config):
     return asdict(config)
+
+
+# ---------------------------------------------------------------------------
+# Session files and device-resident session pools.
+# ---------------------------------------------------------------------------
+SESSION_FORMAT = 'neurogen-session-v2'
+
+
+def session_payload(state, logits, checkpoint_id, extras=None):
+    """One session in the layout ``Session.save`` writes (neurogen/language/runtime.py:95-100).
+
+    ``state`` is the model state of one session in the reference tuple layout (batch 1) and
+    ``logits`` its last logits [264].  The text decoder, sampling generator and audio front-end
+    fields take the values a fresh ``Session`` holds (runtime.py:22-37) unless ``extras`` gives
+    them, so the reference runtime can load the file and continue the conversation.
+    """
+    payload = {'format': SESSION_FORMAT, 'checkpoint_id': checkpoint_id, 'state': state,
+               'logits': torch.as_tensor(logits, dtype=torch.float32),
+               'random': torch.Generator().manual_seed(1).get_state(), 'decoder': ([], 0),
+               'audio_state': None, 'previous_ctc': PAD, 'audio_decoder': ([], 0),
+               'audio_buffer': torch.empty(0), 'audio_emitted': False}
+    payload.update(extras or {})
+    return payload
+
+
+def save_session(path, payload):
+    """Atomic write (temporary file, then rename), as training.py:31-36 does."""
+    from pathlib import Path
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    temporary = path.with_name(path.name + '.tmp')
+    torch.save(payload, temporary)
+    temporary.replace(path)
+
+
+def load_session(path, checkpoint_id):
+    """A session file of this checkpoint; the reference's check and message (runtime.py:103-106)."""
+    payload = torch.load(path, map_location='cpu', weights_only=True)
+    if payload.get('format') != SESSION_FORMAT or payload.get('checkpoint_id') != checkpoint_id:
+        raise ValueError('Session belongs to a different model checkpoint')
+    return payload
+
+
+class SessionPool:
+    """``sessions`` independent streaming sessions whose states stay on the GPU (``ng_pool_*``).
+
+    ``step(tokens)`` feeds one token to every session (one CUDA-graph replay) and returns the
+    logits [sessions, 264].  ``save``/``load`` move one session to or from a
+    ``neurogen-session-v2`` file in the reference's layout, so a conversation can move between
+    this pool and the reference runtime.
+    """
+
+    def __init__(self, model, sessions):
+        self.model = model
+        self.lib = model.engine.lib
+        self.sessions = int(sessions)
+        self.h = self.lib.ng_pool_create(model.engine.handle, self.sessions)
+        if not self.h:
+            raise ValueError(self.lib.ng_error().decode())
+        self.logits = np.zeros((self.sessions, VOCAB), np.float32)
+
+    def close(self):
+        if getattr(self, 'h', None):
+            self.lib.ng_pool_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, code):
+        if code:
+            raise ValueError(self.lib.ng_error().decode())
+
+    def step(self, tokens):
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        if tokens.shape != (self.sessions,):
+            raise ValueError(f'Need one token per session ({self.sessions})')
+        self._check(self.lib.ng_pool_step(self.h, tokens, self.logits.ctypes.data, None, None))
+        return self.logits.copy()
+
+    def states(self):
+        """Packed states [sessions, state_size] in the reference order."""
+        out = np.empty((self.sessions, self.model.engine.state_size), np.float32)
+        self._check(self.lib.ng_pool_store(self.h, out))
+        return out
+
+    def set_states(self, packed):
+        packed = np.ascontiguousarray(packed, dtype=np.float32)
+        if packed.shape != (self.sessions, self.model.engine.state_size):
+            raise ValueError('Invalid native state size')
+        self._check(self.lib.ng_pool_load(self.h, packed))
+
+    def save(self, path, index, checkpoint_id, extras=None):
+        """Session ``index`` to a session file."""
+        state = self.model.unpack_state(self.states()[index:index + 1])
+        save_session(path, session_payload(state, self.logits[index], checkpoint_id, extras))
+
+    def load(self, path, index, checkpoint_id):
+        """A session file into session ``index``; returns the payload (decoder, audio fields)."""
+        payload = load_session(path, checkpoint_id)
+        packed = self.states()
+        packed[index] = self.model.pack_state(payload['state'], 1)[0]
+        self.set_states(packed)
+        self.logits[index] = np.asarray(payload['logits'], np.float32).reshape(VOCAB)
+        return payload

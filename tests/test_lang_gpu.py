@@ -279,3 +279,31 @@ def test_tick_paths_match_reference(columns, ticks, batch):
             lr, sr[b], ar, hr = ref.step(int(toks[b]), sr[b])
             np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
             assert_state_close(cfg, sb[b], sr[b])
+
+
+def test_session_pool_save_load_roundtrip(tmp_path):
+    """A session saved from a device pool in the reference's session layout and loaded into
+    another pool (any slot) continues exactly as the original."""
+    from neurogen_b200.language import (LanguageConfig, NativeLanguageModel, SessionPool, init_packed_weights,
+                                        load_session)
+    cfg = LanguageConfig(columns=4, width=32, regions=2, ticks=2, idle_steps=1)
+    model = NativeLanguageModel(cfg, init_packed_weights(cfg, seed=3))
+    a = SessionPool(model, 4)
+    rng = np.random.default_rng(0)
+    for _ in range(5):
+        a.step(rng.integers(0, 264, 4))
+    a.save(tmp_path / 's.pt', 2, 'ckpt-1')
+    payload = load_session(tmp_path / 's.pt', 'ckpt-1')
+    assert payload['format'] == 'neurogen-session-v2' and len(payload['state']) == cfg.regions
+    assert tuple(payload['state'][0][4].shape) == (1, cfg.width)
+    with pytest.raises(ValueError, match='different model checkpoint'):
+        load_session(tmp_path / 's.pt', 'ckpt-2')
+    b = SessionPool(model, 3)
+    b.load(tmp_path / 's.pt', 0, 'ckpt-1')
+    assert np.array_equal(b.logits[0], a.logits[2])
+    for _ in range(4):
+        toks = rng.integers(0, 264, 4)
+        la = a.step(toks)
+        lb = b.step(np.array([toks[2], 7, 9]))
+        assert np.array_equal(la[2], lb[0])
+    assert np.array_equal(a.states()[2], b.states()[0])

@@ -258,3 +258,36 @@ def test_device_generation_checks_the_ring_range():
         Topology(cfg)
     with pytest.raises(ValueError, match='fixed-point range'):
         Network(cfg)
+
+
+STALL_CHILD = r'''
+import os, sys
+sys.path[:0] = [{root!r}, {pkg!r}]
+from neurogen_b200.network import Network, Topology, isolated_8k
+os.environ['NEUROGEN_TEST_RESIDENT_STALL'] = '1'
+net = Topology(isolated_8k()).network()
+assert net.launch == 'resident'
+try:
+    net.run(10)
+except ValueError as e:
+    print('raised:', e)
+del os.environ['NEUROGEN_TEST_RESIDENT_STALL']
+ok = Topology(isolated_8k()).network()   # the context is still usable
+s, c = ok.run(20)
+print('after:', int(c[:, 0].sum()))
+'''
+
+
+def test_resident_barrier_wait_runs_out_cleanly(tmp_path):
+    """The grid barrier's wait is bounded: with an unreachable target every CTA gives up after its
+    limit, the host raises, and the same process creates and runs a new network afterwards."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    script = tmp_path / 'stall.py'
+    script.write_text(STALL_CHILD.format(root=str(root), pkg=str(root / 'neurogen-2.5_b200')))
+    out = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-3000:]
+    assert 'raised:' in out.stdout and 'timed out' in out.stdout
+    assert 'after:' in out.stdout and int(out.stdout.split('after:')[1]) > 0
