@@ -55,6 +55,8 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--ticks', type=int, default=0, help='override ticks per step (profiling runs)')
     p.add_argument('--tokens', type=int, default=0, help='override tokens per step (profiling runs)')
+    p.add_argument('--sessions', type=int, default=0,
+                   help='sessions workload: override the 256 sessions (profiling runs, e.g. one rank\'s share)')
     return p.parse_args()
 
 
@@ -410,7 +412,7 @@ def bench_lang(args, dist):
     if args.workload == 'bc250':
         mine = [0]
     else:
-        per = SESSIONS // dist.world
+        per = (args.sessions or SESSIONS) // dist.world
         mine = list(range(dist.rank * per, (dist.rank + 1) * per))
     B = len(mine)
     T = args.tokens or LANG_TOKENS_PER_STEP[args.workload]
@@ -448,7 +450,7 @@ def bench_lang(args, dist):
         'higher_is_better': True, 'scaling': 'strong' if args.workload == 'sessions' else 'weak',
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic',
         'config': {'workload': 'bc250_batch1' if args.workload == 'bc250' else 'bc250_sessions256',
-                   'sessions': SESSIONS if args.workload == 'sessions' else 1, 'tokens_per_step': T,
+                   'sessions': (args.sessions or SESSIONS) if args.workload == 'sessions' else 1, 'tokens_per_step': T,
                    'sessions_per_gpu': B, 'weights': 'seed-0 random init (packed 14,804,744 fp32)',
                    'l2': 'weights (59 MB) L2-resident by design', 'parallelism': f'dp{dist.world}'},
         'roofline': {'bound': 'tensor', 'achieved': achieved, 'peak': pk.get('bf16_tflops'),

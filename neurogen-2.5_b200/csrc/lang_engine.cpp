@@ -158,11 +158,14 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
     g.rec = upload(rec);
     const float *in_w = take(c * d.n_in * w);
     g.in_wp = upload(to_panels(in_w, c * d.n_in, w));
+    g.in_wr = upload(in_w, c * d.n_in * w);
     g.in_b = upload(take(c * d.n_in), c * d.n_in);
     const float *fb_w = take(c * d.n_fb * w);
     g.fb_wp = upload(to_panels(fb_w, c * d.n_fb, w));
+    g.fb_wr = upload(fb_w, c * d.n_fb * w);
     const float *out_w = take(w * c * d.n_out * 2);
     g.out_wp = upload(to_panels(out_w, w, c * d.n_out * 2));
+    g.out_wr = upload(out_w, w * c * d.n_out * 2);
     g.out_b = upload(take(w), w);
     g.norm_w = upload(take(w), w);
     g.norm_b = upload(take(w), w);
@@ -173,6 +176,7 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   }
   const float *head_w = take(size_t(kVocab) * w);
   head_wp = upload(to_panels(head_w, kVocab, w));
+  head_wr = upload(head_w, size_t(kVocab) * w);
   head_b = upload(take(kVocab), kVocab);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
 }
@@ -200,6 +204,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
         const int r = r0 + z;
         ProjArgs &fa = fb.a[z];
         fa.wp = regions[r].fb_wp.as<float>();
+        fa.wr = regions[r].fb_wr.as<float>();
         fa.x = d_state + r * d.RS + 4L * d.n;
         fa.ldx = d.S;
         fa.y = sc.fb + size_t(r) * B * Mfb;
@@ -217,6 +222,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       if (sensory) {
         ProjArgs ia{};
         ia.wp = g.in_wp.as<float>();
+        ia.wr = g.in_wr.as<float>();
         ia.bias = g.in_b.as<float>();
         if (r == 0) {
           ia.x = d_tokens ? emb.as<float>() : d_inputs;
@@ -263,6 +269,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       }
       ProjArgs oa{};
       oa.wp = g.out_wp.as<float>();
+      oa.wr = g.out_wr.as<float>();
       oa.bias = g.out_b.as<float>();
       oa.x = sc.feat;
       oa.ldx = Kout;
@@ -292,6 +299,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
   if (d_logits) {
     ProjArgs ha{};
     ha.wp = head_wp.as<float>();
+    ha.wr = head_wr.as<float>();
     ha.bias = head_b.as<float>();
     ha.x = sc.h;
     ha.ldx = d.w;

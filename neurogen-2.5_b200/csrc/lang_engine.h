@@ -26,6 +26,7 @@ struct RegionWeights {
   DeviceBuffer in_wp, in_b;             // panels of [c*n_in][w], bias
   DeviceBuffer fb_wp;                   // panels of [c*n_fb][w]
   DeviceBuffer out_wp, out_b;           // panels of [w][c*n_out*2], bias
+  DeviceBuffer in_wr, fb_wr, out_wr;    // the same three row-major (small-batch kernel)
   DeviceBuffer norm_w, norm_b, decay;   // [w]
 };
 
@@ -75,7 +76,7 @@ public:
   std::string label;
   cudaStream_t stream = nullptr;
   UnitTables tables;
-  DeviceBuffer emb, head_wp, head_b;
+  DeviceBuffer emb, head_wp, head_b, head_wr;
   std::vector<RegionWeights> regions;
   Scratch host_scratch; // used by the host-buffer entry points (under the engine mutex)
 };

@@ -269,6 +269,180 @@ __global__ void __launch_bounds__(gemm_threads<BN, TN>()) k_gemm(ProjBatch pb) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Projection, small batch (2..64 sessions a launch column): 256 threads a CTA,
+// thread (r, s) = (tid / BS, tid % BS) owns the one chain of row r0 + r and
+// session b0 + s, so a 32-session tile gives a 768-row projection 768 warps.
+// The CTA's 256/BS rows (a slice of one 32-row panel) and BS sessions stream
+// through an 8-stage x 64-k cp.async ring, deep enough to cover L2 latency
+// with few warps an SM.  Same sequential chain per output as every other
+// projection kernel: results are bit-identical.
+// ---------------------------------------------------------------------------
+constexpr int SB_KC = 64, SB_STAGES = 8, SB_THREADS = 256;
+template <int BS> __host__ __device__ constexpr int sb_rows() { return SB_THREADS / BS; }
+template <int BS> __host__ __device__ constexpr int sb_stage_floats() { return SB_KC * (sb_rows<BS>() + BS); }
+
+template <int BS>
+__global__ void __launch_bounds__(SB_THREADS) k_gemm_sb(ProjBatch pb) {
+  constexpr int RB = sb_rows<BS>(), STAGE = sb_stage_floats<BS>();
+  extern __shared__ __align__(16) float sm[];
+  const ProjArgs &a = pb.a[blockIdx.z];
+  const int m0 = blockIdx.x * RB, b0 = blockIdx.y * BS;
+  if (m0 >= a.M || b0 >= a.B) return;
+  const int tid = threadIdx.x, r = tid / BS, s = tid % BS;
+  const int p = m0 >> 5, r0 = m0 & 31; // panel and row offset inside it
+  const float *wq = a.wp + (size_t)p * a.K * 32 + r0;
+  const int nch = (a.K + SB_KC - 1) / SB_KC;
+  auto issue = [&](int ch) {
+    if (ch < nch) {
+      const int k0 = ch * SB_KC, kc = min(SB_KC, a.K - k0);
+      float *ws = sm + (ch % SB_STAGES) * STAGE;
+      float *xs = ws + SB_KC * RB;
+      constexpr int PIECES = RB / 4; // 16-byte pieces of a k's RB weights
+      for (int i = tid; i < kc * PIECES; i += SB_THREADS) {
+        const int k = i / PIECES, q = i - k * PIECES;
+        cp_async16(ws + k * RB + q * 4, wq + (size_t)(k0 + k) * 32 + q * 4);
+      }
+      for (int i = tid; i < kc * BS; i += SB_THREADS) {
+        const int sidx = i / kc, k = i - sidx * kc, b = b0 + sidx;
+        if (b < a.B) cp_async4(xs + k * BS + sidx, a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx + k0 + k);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int st = 0; st < SB_STAGES - 1; ++st) issue(st);
+  const int m = m0 + r, b = b0 + s;
+  float acc = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+  for (int ch = 0; ch < nch; ++ch) {
+    issue(ch + SB_STAGES - 1);
+    cp_async_wait<SB_STAGES - 1>();
+    __syncthreads();
+    const float *ws = sm + (ch % SB_STAGES) * STAGE;
+    const float *xs = ws + SB_KC * RB;
+    const int kc = min(SB_KC, a.K - ch * SB_KC);
+    if (kc == SB_KC) {
+      // 16 independent products, then their 16 dependent adds.
+#pragma unroll
+      for (int g = 0; g < SB_KC; g += 16) {
+        float pr[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pr[j] = __fmul_rn(ws[(g + j) * RB + r], xs[(g + j) * BS + s]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, pr[j]);
+      }
+    } else {
+      for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(ws[k * RB + r], xs[k * BS + s]));
+    }
+    __syncthreads();
+  }
+  if (m < a.M && b < a.B) {
+    if (a.addv) acc = __fadd_rn(acc, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
+    a.y[(long)b * a.ldy + m] = acc;
+  }
+}
+
+template <int BS> size_t gemm_sb_smem() { return sizeof(float) * SB_STAGES * sb_stage_floats<BS>(); }
+
+// ---------------------------------------------------------------------------
+// Projection from row-major weights: CTA = RB rows x BS sessions, one chain a
+// thread.  Both operands stage along k in 16-byte cp.async pieces (weight rows
+// W[m][k..], session inputs x[b][k..]) into rows padded to 68 floats, so a
+// thread reads four k of its row and of its session with two conflict-free
+// 128-bit loads.  8-stage x 64-k ring.  Same sequential chain per output:
+// bit-identical to the other projection kernels.  Needs K, ldx and the bases
+// 16-byte aligned (checked by the launcher).
+// ---------------------------------------------------------------------------
+constexpr int RM_KC = 64, RM_STAGES = 8, RM_LD = RM_KC + 4;
+template <int RB, int BS> __host__ __device__ constexpr int rm_stage_floats() { return (RB + BS) * RM_LD; }
+
+template <int RB, int BS>
+__global__ void __launch_bounds__(RB * BS) k_gemm_rm(ProjBatch pb) {
+  constexpr int NT = RB * BS, STAGE = rm_stage_floats<RB, BS>();
+  extern __shared__ __align__(16) float sm[];
+  const ProjArgs &a = pb.a[blockIdx.z];
+  const int m0 = blockIdx.x * RB, b0 = blockIdx.y * BS;
+  if (m0 >= a.M || b0 >= a.B) return;
+  const int tid = threadIdx.x, r = tid / BS, s = tid % BS;
+  const int nch = (a.K + RM_KC - 1) / RM_KC;
+  auto issue = [&](int ch) {
+    if (ch < nch) {
+      const int k0 = ch * RM_KC, pieces = min(RM_KC, a.K - k0) / 4;
+      float *ws = sm + (ch % RM_STAGES) * STAGE;
+      float *xs = ws + RB * RM_LD;
+      for (int i = tid; i < RB * pieces; i += NT) {
+        const int rr = i / pieces, q = i - rr * pieces;
+        if (m0 + rr < a.M) cp_async16(ws + rr * RM_LD + q * 4, a.wr + (size_t)(m0 + rr) * a.K + k0 + q * 4);
+      }
+      for (int i = tid; i < BS * pieces; i += NT) {
+        const int ss = i / pieces, q = i - ss * pieces, b = b0 + ss;
+        if (b < a.B)
+          cp_async16(xs + ss * RM_LD + q * 4, a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx + k0 + q * 4);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int st = 0; st < RM_STAGES - 1; ++st) issue(st);
+  const int m = m0 + r, b = b0 + s;
+  float acc = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+  for (int ch = 0; ch < nch; ++ch) {
+    issue(ch + RM_STAGES - 1);
+    cp_async_wait<RM_STAGES - 1>();
+    __syncthreads();
+    const float *wrow = sm + (ch % RM_STAGES) * STAGE + r * RM_LD;
+    const float *xrow = sm + (ch % RM_STAGES) * STAGE + RB * RM_LD + s * RM_LD;
+    const int kc = min(RM_KC, a.K - ch * RM_KC);
+    if (kc == RM_KC) {
+#pragma unroll
+      for (int g = 0; g < RM_KC; g += 16) {
+        float pr[16];
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          const float4 wv = *reinterpret_cast<const float4 *>(wrow + g + j);
+          const float4 xv = *reinterpret_cast<const float4 *>(xrow + g + j);
+          pr[j] = __fmul_rn(wv.x, xv.x);
+          pr[j + 1] = __fmul_rn(wv.y, xv.y);
+          pr[j + 2] = __fmul_rn(wv.z, xv.z);
+          pr[j + 3] = __fmul_rn(wv.w, xv.w);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, pr[j]);
+      }
+    } else {
+      for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(wrow[k], xrow[k]));
+    }
+    __syncthreads();
+  }
+  if (m < a.M && b < a.B) {
+    if (a.addv) acc = __fadd_rn(acc, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
+    a.y[(long)b * a.ldy + m] = acc;
+  }
+}
+
+template <int RB, int BS> size_t gemm_rm_smem() { return sizeof(float) * RM_STAGES * rm_stage_floats<RB, BS>(); }
+
+template <int RB, int BS> void run_gemm_rm(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
+  dim3 grid((max_m + RB - 1) / RB, (max_b + BS - 1) / BS, pb.count);
+  k_gemm_rm<RB, BS><<<grid, RB * BS, gemm_rm_smem<RB, BS>(), s>>>(pb);
+}
+
+// Row-major operands usable: weights given, K, ldx and the bases 16-byte aligned.
+bool rm_ok(const ProjBatch &pb) {
+  for (int z = 0; z < pb.count; ++z) {
+    const ProjArgs &a = pb.a[z];
+    if (!a.wr || a.K % 4 || a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.wr) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.x) & 15))
+      return false;
+  }
+  return true;
+}
+
+template <int BS> void run_gemm_sb(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
+  dim3 grid((max_m + sb_rows<BS>() - 1) / sb_rows<BS>(), (max_b + BS - 1) / BS, pb.count);
+  k_gemm_sb<BS><<<grid, SB_THREADS, gemm_sb_smem<BS>(), s>>>(pb);
+}
+
 template <int BN, int TN> size_t gemm_smem() { return sizeof(float) * GM_STAGES * gemm_stage_floats<BN>(); }
 
 template <int BN, int TN> void configure_gemm() {
@@ -542,6 +716,11 @@ void configure_lang_kernels() {
   configure_gemm<16, 2>();
   configure_gemm<32, 4>();
   configure_gemm<64, 4>();
+  cudaFuncSetAttribute(k_gemm_rm<16, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rm_smem<16, 8>());
+  cudaFuncSetAttribute(k_gemm_rm<32, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rm_smem<32, 8>());
+  cudaFuncSetAttribute(k_gemm_sb<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_sb_smem<8>());
+  cudaFuncSetAttribute(k_gemm_sb<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_sb_smem<16>());
+  cudaFuncSetAttribute(k_gemm_sb<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_sb_smem<32>());
   cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)(sizeof(float) * GV_STAGES * GV_STAGE_FLOATS));
 }
@@ -549,6 +728,11 @@ void configure_lang_kernels() {
 void preload_lang_kernels() {
   cudaFuncAttributes fa;
   const void *kernels[] = {(const void *)k_gemv,
+                           (const void *)k_gemm_rm<16, 8>,
+                           (const void *)k_gemm_rm<32, 8>,
+                           (const void *)k_gemm_sb<8>,
+                           (const void *)k_gemm_sb<16>,
+                           (const void *)k_gemm_sb<32>,
                            (const void *)k_gemm<8, 1>,
                            (const void *)k_gemm<16, 2>,
                            (const void *)k_gemm<32, 4>,
@@ -588,6 +772,28 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s) {
     const char *v = std::getenv("NEUROGEN_PROJ_TILE");
     return v ? std::atoi(v) : 0;
   }();
+  // NEUROGEN_PROJ_SMALL = 8 | 16 | 32 forces the small-batch kernel's session
+  // tile the same way.
+  static const int forced_small = [] {
+    const char *v = std::getenv("NEUROGEN_PROJ_SMALL");
+    return v ? std::atoi(v) : 0;
+  }();
+  // NEUROGEN_PROJ_ROWMAJOR = 16 | 32 forces the row-major kernel with that
+  // many rows a CTA (when its operands qualify).
+  static const int forced_rm = [] {
+    const char *v = std::getenv("NEUROGEN_PROJ_ROWMAJOR");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (forced_rm && rm_ok(pb)) {
+    if (forced_rm == 32) return run_gemm_rm<32, 8>(pb, max_m, max_b, s);
+    return run_gemm_rm<16, 8>(pb, max_m, max_b, s);
+  }
+  switch (forced_small) {
+  case 8: return run_gemm_sb<8>(pb, max_m, max_b, s);
+  case 16: return run_gemm_sb<16>(pb, max_m, max_b, s);
+  case 32: return run_gemm_sb<32>(pb, max_m, max_b, s);
+  default: break;
+  }
   switch (forced) {
   case 8: return run_gemm<8, 1>(pb, max_m, max_b, s);
   case 16: return run_gemm<16, 2>(pb, max_m, max_b, s);
@@ -595,6 +801,14 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s) {
   case 64: return run_gemm<64, 4>(pb, max_m, max_b, s);
   default: break;
   }
+  // Row-major operands (the engine's default): 16 rows x 8 sessions a CTA,
+  // measured fastest at every batch on BC-250 (32 / 64 / 128 / 256 sessions:
+  // 44.0 K / 71.0 K / 88.3 K / 104.4 K tokens/s, against 36.8 K / 50.4 K /
+  // 74.6 K / 92.7 K with the panel kernels).
+  if (rm_ok(pb)) return run_gemm_rm<16, 8>(pb, max_m, max_b, s);
+  // Up to 64 sessions: one chain a thread (small-batch kernel) on whole
+  // 32-row panels x 8 sessions, so each session input is staged once a panel.
+  if (max_b <= 64) return run_gemm_sb<8>(pb, max_m, max_b, s);
   if (max_b > 32 && warps(64, gemm_threads<64, 4>()) >= want) run_gemm<64, 4>(pb, max_m, max_b, s);
   else if (max_b > 16 && warps(32, gemm_threads<32, 4>()) >= want) run_gemm<32, 4>(pb, max_m, max_b, s);
   else if (max_b > 8 && warps(16, gemm_threads<16, 2>()) >= want) run_gemm<16, 2>(pb, max_m, max_b, s);

@@ -23,6 +23,7 @@ struct UnitTables {
 // Row b of x is x + (xidx ? xidx[b] : b) * ldx.
 struct ProjArgs {
   const float *wp;
+  const float *wr;   // the same weights row-major [M][K] (small-batch kernel), or null
   const float *bias; // [M] or null
   const float *x;
   const int *xidx; // optional row gather (embedding lookup)

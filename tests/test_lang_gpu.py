@@ -223,11 +223,13 @@ def test_pool_matches_host_batch():
         lib.ng_pool_destroy(pool)
 
 
-@pytest.mark.parametrize('tile', ['8', '16', '32', '64'])
-def test_every_projection_tile_is_bit_identical(tile):
-    """Each session tile of the batched projection gives the same bits as the batch-1 kernel
-    (one sequential chain per output in every case).  Runs in a child process because the
-    tile override is read once per process."""
+@pytest.mark.parametrize('var,tile', [('NEUROGEN_PROJ_TILE', t) for t in ('8', '16', '32', '64')] +
+                         [('NEUROGEN_PROJ_SMALL', t) for t in ('8', '16', '32')] +
+                         [('NEUROGEN_PROJ_ROWMAJOR', t) for t in ('16', '32')])
+def test_every_projection_tile_is_bit_identical(var, tile):
+    """Each session tile of the batched projection kernels (wide tiles and the small-batch
+    kernel) gives the same bits as the batch-1 kernel (one sequential chain per output in every
+    case).  Runs in a child process because the tile override is read once per process."""
     import os
     import subprocess
     import sys
@@ -250,7 +252,7 @@ for t in range(3):
         assert np.array_equal(l1[0], lb[b]) and np.array_equal(s1[0], sb[b]), (t, b)
 print('ok')
 """
-    env = dict(os.environ, NEUROGEN_PROJ_TILE=tile)
+    env = dict(os.environ, **{var: tile})
     out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0 and 'ok' in out.stdout, out.stderr[-2000:]
 
