@@ -345,78 +345,104 @@ __global__ void __launch_bounds__(SB_THREADS) k_gemm_sb(ProjBatch pb) {
 template <int BS> size_t gemm_sb_smem() { return sizeof(float) * SB_STAGES * sb_stage_floats<BS>(); }
 
 // ---------------------------------------------------------------------------
-// Projection from row-major weights: CTA = RB rows x BS sessions, one chain a
-// thread.  Both operands stage along k in 16-byte cp.async pieces (weight rows
-// W[m][k..], session inputs x[b][k..]) into rows padded to 68 floats, so a
-// thread reads four k of its row and of its session with two conflict-free
-// 128-bit loads.  8-stage x 64-k ring.  Same sequential chain per output:
-// bit-identical to the other projection kernels.  Needs K, ldx and the bases
-// 16-byte aligned (checked by the launcher).
+// Projection from row-major weights: CTA = RB rows x BS sessions; thread
+// (r, s) owns the chains of row r for sessions s and s + BS/2, added as one
+// add.rn.f32x2 pair (products stay scalar __fmul_rn).  Both operands stage
+// along k in 16-byte cp.async pieces (weight rows W[m][k..], session inputs
+// x[b][k..]) into rows padded to 68 floats, so each thread reads four k of
+// its row and of its two sessions with three conflict-free 128-bit loads;
+// the copy sources of each thread are fixed and computed once.  8-stage x
+// 64-k ring.  Same sequential chain per output: bit-identical to the other
+// projection kernels.  Needs K, ldx and the bases 16-byte aligned (checked by
+// the launcher).
 // ---------------------------------------------------------------------------
 constexpr int RM_KC = 64, RM_STAGES = 8, RM_LD = RM_KC + 4;
 template <int RB, int BS> __host__ __device__ constexpr int rm_stage_floats() { return (RB + BS) * RM_LD; }
+template <int RB, int BS> __host__ __device__ constexpr int rm_threads() { return RB * BS / 2; }
 
 template <int RB, int BS>
-__global__ void __launch_bounds__(RB * BS) k_gemm_rm(ProjBatch pb) {
-  constexpr int NT = RB * BS, STAGE = rm_stage_floats<RB, BS>();
+__global__ void __launch_bounds__(rm_threads<RB, BS>()) k_gemm_rm(ProjBatch pb) {
+  constexpr int NT = rm_threads<RB, BS>(), STAGE = rm_stage_floats<RB, BS>(), HB = BS / 2;
+  constexpr int PIECES = RM_KC / 4;                     // 16-byte pieces of a row's 64 k
+  constexpr int WP = RB * PIECES / NT, XP = BS * PIECES / NT; // pieces a thread copies
+  static_assert(RB * PIECES % NT == 0 && BS * PIECES % NT == 0, "tile");
   extern __shared__ __align__(16) float sm[];
   const ProjArgs &a = pb.a[blockIdx.z];
   const int m0 = blockIdx.x * RB, b0 = blockIdx.y * BS;
   if (m0 >= a.M || b0 >= a.B) return;
-  const int tid = threadIdx.x, r = tid / BS, s = tid % BS;
+  const int tid = threadIdx.x, r = tid / HB, s = tid % HB;
   const int nch = (a.K + RM_KC - 1) / RM_KC;
+  // Fixed copy assignment: piece i -> (row or session i / PIECES, piece i % PIECES).
+  const float *wsrc[WP], *xsrc[XP];
+  int wdst[WP], xdst[XP];
+  bool wok[WP], xok[XP];
+#pragma unroll
+  for (int j = 0; j < WP; ++j) {
+    const int i = tid + j * NT, rr = i / PIECES, q = i % PIECES;
+    wok[j] = m0 + rr < a.M;
+    wsrc[j] = a.wr + (size_t)(wok[j] ? m0 + rr : 0) * a.K + q * 4;
+    wdst[j] = rr * RM_LD + q * 4;
+  }
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int i = tid + j * NT, ss = i / PIECES, q = i % PIECES, b = b0 + ss;
+    xok[j] = b < a.B;
+    xsrc[j] = a.x + (long)(xok[j] ? (a.xidx ? a.xidx[b] : b) : 0) * a.ldx + q * 4;
+    xdst[j] = RB * RM_LD + ss * RM_LD + q * 4;
+  }
   auto issue = [&](int ch) {
     if (ch < nch) {
-      const int k0 = ch * RM_KC, pieces = min(RM_KC, a.K - k0) / 4;
-      float *ws = sm + (ch % RM_STAGES) * STAGE;
-      float *xs = ws + RB * RM_LD;
-      for (int i = tid; i < RB * pieces; i += NT) {
-        const int rr = i / pieces, q = i - rr * pieces;
-        if (m0 + rr < a.M) cp_async16(ws + rr * RM_LD + q * 4, a.wr + (size_t)(m0 + rr) * a.K + k0 + q * 4);
-      }
-      for (int i = tid; i < BS * pieces; i += NT) {
-        const int ss = i / pieces, q = i - ss * pieces, b = b0 + ss;
-        if (b < a.B)
-          cp_async16(xs + ss * RM_LD + q * 4, a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx + k0 + q * 4);
-      }
+      const int k0 = ch * RM_KC, kend = a.K - k0; // pieces at q*4 < kend are in range
+      float *st = sm + (ch % RM_STAGES) * STAGE;
+#pragma unroll
+      for (int j = 0; j < WP; ++j)
+        if (wok[j] && (wdst[j] % RM_LD) < kend) cp_async16(st + wdst[j], wsrc[j] + k0);
+#pragma unroll
+      for (int j = 0; j < XP; ++j)
+        if (xok[j] && ((xdst[j] - RB * RM_LD) % RM_LD) < kend) cp_async16(st + xdst[j], xsrc[j] + k0);
     }
     cp_async_commit();
   };
 #pragma unroll
   for (int st = 0; st < RM_STAGES - 1; ++st) issue(st);
-  const int m = m0 + r, b = b0 + s;
-  float acc = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+  const int m = m0 + r, b_lo = b0 + s, b_hi = b0 + s + HB;
+  const float bias = (a.bias && m < a.M) ? a.bias[m] : 0.f;
+  f32x2 acc = pack2(bias, bias); // (session s, session s + BS/2)
   for (int ch = 0; ch < nch; ++ch) {
     issue(ch + RM_STAGES - 1);
     cp_async_wait<RM_STAGES - 1>();
     __syncthreads();
-    const float *wrow = sm + (ch % RM_STAGES) * STAGE + r * RM_LD;
-    const float *xrow = sm + (ch % RM_STAGES) * STAGE + RB * RM_LD + s * RM_LD;
+    const float *st = sm + (ch % RM_STAGES) * STAGE;
+    const float *wrow = st + r * RM_LD, *xlo = st + RB * RM_LD + s * RM_LD, *xhi = xlo + HB * RM_LD;
     const int kc = min(RM_KC, a.K - ch * RM_KC);
     if (kc == RM_KC) {
 #pragma unroll
-      for (int g = 0; g < RM_KC; g += 16) {
-        float pr[16];
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const float4 wv = *reinterpret_cast<const float4 *>(wrow + g + j);
-          const float4 xv = *reinterpret_cast<const float4 *>(xrow + g + j);
-          pr[j] = __fmul_rn(wv.x, xv.x);
-          pr[j + 1] = __fmul_rn(wv.y, xv.y);
-          pr[j + 2] = __fmul_rn(wv.z, xv.z);
-          pr[j + 3] = __fmul_rn(wv.w, xv.w);
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc = __fadd_rn(acc, pr[j]);
+      for (int q = 0; q < RM_KC / 4; ++q) {
+        const float4 wv = *reinterpret_cast<const float4 *>(wrow + 4 * q);
+        const float4 xl = *reinterpret_cast<const float4 *>(xlo + 4 * q);
+        const float4 xh = *reinterpret_cast<const float4 *>(xhi + 4 * q);
+        acc = add2(acc, pack2(__fmul_rn(wv.x, xl.x), __fmul_rn(wv.x, xh.x)));
+        acc = add2(acc, pack2(__fmul_rn(wv.y, xl.y), __fmul_rn(wv.y, xh.y)));
+        acc = add2(acc, pack2(__fmul_rn(wv.z, xl.z), __fmul_rn(wv.z, xh.z)));
+        acc = add2(acc, pack2(__fmul_rn(wv.w, xl.w), __fmul_rn(wv.w, xh.w)));
       }
     } else {
-      for (int k = 0; k < kc; ++k) acc = __fadd_rn(acc, __fmul_rn(wrow[k], xrow[k]));
+      for (int k = 0; k < kc; ++k)
+        acc = add2(acc, pack2(__fmul_rn(wrow[k], xlo[k]), __fmul_rn(wrow[k], xhi[k])));
     }
     __syncthreads();
   }
-  if (m < a.M && b < a.B) {
-    if (a.addv) acc = __fadd_rn(acc, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
-    a.y[(long)b * a.ldy + m] = acc;
+  float lo, hi;
+  unpack2(acc, lo, hi);
+  if (m < a.M) {
+    if (b_lo < a.B) {
+      if (a.addv) lo = __fadd_rn(lo, __fmul_rn(0.25f, a.addv[(long)b_lo * a.ldadd + m]));
+      a.y[(long)b_lo * a.ldy + m] = lo;
+    }
+    if (b_hi < a.B) {
+      if (a.addv) hi = __fadd_rn(hi, __fmul_rn(0.25f, a.addv[(long)b_hi * a.ldadd + m]));
+      a.y[(long)b_hi * a.ldy + m] = hi;
+    }
   }
 }
 
@@ -424,7 +450,7 @@ template <int RB, int BS> size_t gemm_rm_smem() { return sizeof(float) * RM_STAG
 
 template <int RB, int BS> void run_gemm_rm(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
   dim3 grid((max_m + RB - 1) / RB, (max_b + BS - 1) / BS, pb.count);
-  k_gemm_rm<RB, BS><<<grid, RB * BS, gemm_rm_smem<RB, BS>(), s>>>(pb);
+  k_gemm_rm<RB, BS><<<grid, rm_threads<RB, BS>(), gemm_rm_smem<RB, BS>(), s>>>(pb);
 }
 
 // Row-major operands usable: weights given, K, ldx and the bases 16-byte aligned.
