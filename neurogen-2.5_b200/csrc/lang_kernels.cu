@@ -570,9 +570,19 @@ __global__ void __launch_bounds__(64 * CPC * SB) k_ticks_cluster(TickArgs a, int
   const int tid = threadIdx.x, id = tid & 63, cl = (tid >> 6) % CPC, s = tid / (64 * CPC);
   const int col = g * CPC + cl, b = blockIdx.y * SB + s;
   const bool live = b < a.B;
-  for (int i = tid; i < CPC * 4096; i += 64 * CPC * SB) {
-    const int c = i >> 12, r = i & 4095;
-    wt[c * 64 * TK_LD + (r >> 6) * TK_LD + (r & 63)] = a.rec[(size_t)(g * CPC + c) * 4096 + r];
+  {
+    // The CTA's CPC x 4096 recurrent weights: every thread's loads issued
+    // before any store, so the staging costs one L2 round trip.
+    constexpr int NT = 64 * CPC * SB, PER = CPC * 4096 / NT;
+    static_assert(CPC * 4096 % NT == 0, "weight staging");
+    float v[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) v[u] = __ldg(a.rec + (size_t)g * CPC * 4096 + tid + u * NT);
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, c = i >> 12, r = i & 4095;
+      wt[c * 64 * TK_LD + (r >> 6) * TK_LD + (r & 63)] = v[u];
+    }
   }
   const bool exc = (a.tab.exc_mask >> id) & 1ull;
   const int n = a.n, i = col * 64 + id;
