@@ -55,6 +55,8 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--ticks', type=int, default=0, help='override ticks per step (profiling runs)')
     p.add_argument('--tokens', type=int, default=0, help='override tokens per step (profiling runs)')
+    p.add_argument('--neurons', type=int, default=0,
+                   help='partitioned4m: override the 4,194,304 neurons (profiling runs, e.g. one rank\'s share)')
     p.add_argument('--sessions', type=int, default=0,
                    help='sessions workload: override the 256 sessions (profiling runs, e.g. one rank\'s share)')
     return p.parse_args()
@@ -233,6 +235,8 @@ def bench_ticks(args, dist):
     part = args.workload == 'partitioned4m'
     cfg, ticks, wl = tick_config(args.workload, args.rate, dist.rank, dist.world)
     ticks = args.ticks or ticks
+    if part and args.neurons:
+        cfg.n, cfg.n_exc = args.neurons, int(args.neurons * 0.8)
     if not part:
         cfg.seed = cfg.seed + dist.rank  # independent replica per rank
     t0 = time.time()
