@@ -754,6 +754,16 @@ void Network::init_state(const void *nccl_id, bool csr, int max_delay) {
   d.bitmask = bitmask_.as<uint32_t>();
   d.bm_stride = int(bm_words);
   d.totals = totals_.as<unsigned long long>();
+  // Split push shape: a CTA scans 64 bitmask words (2,048 presynaptic neurons)
+  // when the presynaptic population is large, so the grid follows the spikes
+  // rather than the population; lanes take 8 synapses a pass when this
+  // partition's rows are short (under ~300 synapses on average), else 16.
+  d.push_span_words = n_pre_ >= (1 << 20) ? 64 : 8;
+  d.push_chunk = (n_pre_ > 0 && nnz_ / n_pre_ < 300) ? 8 : 16;
+  // NEUROGEN_PUSH_SPAN = 8 | 64 and NEUROGEN_PUSH_CHUNK = 8 | 16 force the
+  // shape (tests: results do not depend on it).
+  if (const char *v = std::getenv("NEUROGEN_PUSH_SPAN")) d.push_span_words = std::atoi(v) == 64 ? 64 : 8;
+  if (const char *v = std::getenv("NEUROGEN_PUSH_CHUNK")) d.push_chunk = std::atoi(v) == 8 ? 8 : 16;
   // Small networks: one fused launch per tick; large or partitioned: split
   // membrane / push, with the bitmask all-gather between them.
   split_ = world_ > 1 || c.launch == 2 || (c.launch == 0 && n_ >= 65536);

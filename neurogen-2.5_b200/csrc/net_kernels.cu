@@ -12,7 +12,7 @@
 //   fused  -- one kernel per tick; the warp that owns a spiking neuron pushes
 //             its synapses.  Cheapest for small networks (one launch).
 //   split  -- k_net_alif updates the neurons and writes the bitmask; then
-//             k_net_push CTA b reads the 8 bitmask words of neuron group b,
+//             k_net_push CTA b reads the 8 (or 64) bitmask words of its span,
 //             lists its spiking neurons (CSR) or non-empty 16-neuron
 //             block-columns (block storage) in shared memory, and its 8 warps
 //             take the items round-robin, each lane with all of its synapse
@@ -58,46 +58,52 @@ __device__ __forceinline__ int deliver(const NetDev &d, long long t, uint32_t wo
 }
 
 // Push all outgoing CSR synapses of `pre` with the whole warp: each lane takes
-// 16 consecutive synapses per pass (four 16-byte index loads and two 16-byte
-// fp16 weight loads, or four for fp32), issued together and streamed past the
-// caches (evict-first) before any delivery.  Rows are padded to multiples of
-// 8 and the arrays carry 16 spare entries, so the loads stay in bounds; the
-// deliveries are masked to the row.
-// seg selects the whole row (0), its delay-1 segment (1) or the rest (2).
+// CH (8 or 16) consecutive synapses per pass (16-byte index and weight loads),
+// issued together and streamed past the caches (evict-first) before any
+// delivery; 8 suits short rows (more lanes busy), 16 long ones (more loads in
+// flight a lane).  Rows are padded to multiples of 8 and the arrays carry 16
+// spare entries, so the loads stay in bounds; the deliveries are masked to the
+// row.  seg selects the whole row (0), its delay-1 segment (1) or the rest (2).
 // Returns this lane's delivered (non-zero) synapse count.
+template <int CH>
 __device__ __forceinline__ int push_row(const NetDev &d, long long t, int pre, int lane, int seg) {
   long long e0 = d.row[pre], e1 = d.row[pre + 1];
   if (seg == 1) e1 = e0 + d.mid[pre];
   else if (seg == 2) e0 += d.mid[pre];
   int delivered = 0;
-  for (long long e = e0 + lane * 16; e < e1; e += 512) {
+  for (long long e = e0 + lane * CH; e < e1; e += 32 * CH) {
     const uint4 *ps = reinterpret_cast<const uint4 *>(d.syn + e);
-    uint4 p[4];
+    uint4 p[CH / 4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) p[q] = __ldcs(ps + q);
-    float w[16];
+    for (int q = 0; q < CH / 4; ++q) p[q] = __ldcs(ps + q);
+    float w[CH];
     if (d.w_half) {
       const uint4 *pw = reinterpret_cast<const uint4 *>(static_cast<const __half *>(d.w) + e);
-      const uint4 w0 = __ldcs(pw), w1 = __ldcs(pw + 1);
-      const uint32_t h[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        w[2 * j] = half_bits(h[j] & 0xFFFFu);
-        w[2 * j + 1] = half_bits(h[j] >> 16);
+      for (int q = 0; q < CH / 8; ++q) {
+        const uint4 wv = __ldcs(pw + q);
+        const uint32_t h[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          w[8 * q + 2 * j] = half_bits(h[j] & 0xFFFFu);
+          w[8 * q + 2 * j + 1] = half_bits(h[j] >> 16);
+        }
       }
     } else {
       const float4 *pw = reinterpret_cast<const float4 *>(static_cast<const float *>(d.w) + e);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < CH / 4; ++q) {
         const float4 f = __ldcs(pw + q);
         w[4 * q] = f.x; w[4 * q + 1] = f.y; w[4 * q + 2] = f.z; w[4 * q + 3] = f.w;
       }
     }
-    const uint32_t word[16] = {p[0].x, p[0].y, p[0].z, p[0].w, p[1].x, p[1].y, p[1].z, p[1].w,
-                               p[2].x, p[2].y, p[2].z, p[2].w, p[3].x, p[3].y, p[3].z, p[3].w};
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (e + j < e1) delivered += deliver(d, t, word[j], w[j]);
+    for (int q = 0; q < CH / 4; ++q) {
+      const uint32_t word[4] = {p[q].x, p[q].y, p[q].z, p[q].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (e + 4 * q + j < e1) delivered += deliver(d, t, word[j], w[4 * q + j]);
+    }
   }
   return delivered;
 }
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
     while (m) {
       const int src = __ffs(m) - 1;
       m &= m - 1;
-      events += push_row(d, t, base + src, lane, 0);
+      events += push_row<16>(d, t, base + src, lane, 0);
     }
   }
   unsigned long long *group = d.totals + kTotalsStride * (size_t)blockIdx.x;
@@ -217,22 +223,27 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + kTotalsStride * (size_t)blockIdx.x, counts);
 }
 
-// CTA b pushes the spikes of neurons [256b, 256b+256): its warps list them
-// from the group's 8 bitmask words and take them round-robin.  SEG selects
-// whole rows (0), delay-1 segments (1) or delay>=2 segments (2).
-template <bool BSR, int SEG>
+// CTA b pushes the spikes of presynaptic neurons [32*SPANW*b, 32*SPANW*(b+1)):
+// warp 0 lists them from the span's SPANW bitmask words (block storage: 8
+// words, listed by 16-neuron block-column) and the warps take them round-
+// robin.  Wide spans (64 words) keep the grid proportional to the work when
+// the presynaptic population is large and each rank's share of a row short.
+// SEG selects whole rows (0), delay-1 segments (1) or delay>=2 segments (2).
+template <bool BSR, int SEG, int SPANW, int CH>
 __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned long long *counts) {
-  __shared__ int items[TB];
-  __shared__ unsigned item_mask[TB / 16];
+  static_assert(!BSR || SPANW == 8, "block storage scans 8 words a CTA");
+  constexpr int SPAN = 32 * SPANW;
+  __shared__ int items[SPAN];
+  __shared__ unsigned item_mask[BSR ? SPAN / 16 : 1];
   __shared__ int n_items;
   const long long t = tick_of(tr);
   const uint32_t *bitmask = d.bitmask + (t & 1) * d.bm_stride;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int base = blockIdx.x * TB;
+  const int base = blockIdx.x * SPAN;
   if (warp == 0) {
-    const int w = base / 32 + (lane & 7);
-    const unsigned word = (lane < WARPS && base + (lane & 7) * 32 < d.n_pre) ? bitmask[w] : 0u;
     if (BSR) {
+      const int w = base / 32 + (lane & 7);
+      const unsigned word = (lane < 8 && base + (lane & 7) * 32 < d.n_pre) ? bitmask[w] : 0u;
       // 16 block-columns per group; lane k < 16 owns half (k & 1) of word k / 2.
       const unsigned wk = __shfl_sync(0xffffffffu, word, (lane >> 1) & 7);
       const unsigned sub = lane < 16 ? ((wk >> (16 * (lane & 1))) & 0xFFFFu) : 0u;
@@ -244,22 +255,20 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
       }
       if (lane == 0) n_items = __popc(has);
     } else {
-      const unsigned cnt = lane < WARPS ? __popc(word) : 0u;
-      unsigned pre = cnt; // inclusive scan over the 8 words
+      // Lane l reads words l and l + 32 of the span (those that exist).
+      const unsigned w0 = (lane < SPANW && base + lane * 32 < d.n_pre) ? bitmask[base / 32 + lane] : 0u;
+      const unsigned w1 = (lane + 32 < SPANW && base + (lane + 32) * 32 < d.n_pre) ? bitmask[base / 32 + lane + 32] : 0u;
+      const unsigned cnt = __popc(w0) + __popc(w1);
+      unsigned pre = cnt; // inclusive scan over the lanes
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
+      for (int o = 1; o < 32; o <<= 1) {
         const unsigned v = __shfl_up_sync(0xffffffffu, pre, o);
         if (lane >= o) pre += v;
       }
-      if (lane < WARPS) {
-        unsigned m = word, at = pre - cnt;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          items[at++] = base + lane * 32 + b;
-        }
-      }
-      if (lane == WARPS - 1) n_items = (int)pre;
+      unsigned at = pre - cnt;
+      for (unsigned m = w0; m; m &= m - 1) items[at++] = base + lane * 32 + (__ffs(m) - 1);
+      for (unsigned m = w1; m; m &= m - 1) items[at++] = base + (lane + 32) * 32 + (__ffs(m) - 1);
+      if (lane == 31) n_items = (int)pre;
     }
   }
   __syncthreads();
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
   unsigned long long events = 0;
   for (int k = warp; k < count; k += WARPS) {
     if (BSR) events += push_block_column(d, t, items[k], item_mask[k], lane, SEG);
-    else events += push_row(d, t, items[k], lane, SEG);
+    else events += push_row<CH>(d, t, items[k], lane, SEG);
   }
   add_block_count(events, d.totals + kTotalsStride * (size_t)blockIdx.x + (SEG == 2 ? 2 : 1),
                   counts ? counts + 1 : nullptr);
@@ -292,17 +301,22 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
   else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
 }
 
+template <bool BSR, int SPANW, int CH>
+void push_seg(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s) {
+  const int span = 32 * SPANW, blocks = (d.n_pre + span - 1) / span;
+  if (seg == 1) k_net_push<BSR, 1, SPANW, CH><<<blocks, TB, 0, s>>>(d, t, counts);
+  else if (seg == 2) k_net_push<BSR, 2, SPANW, CH><<<blocks, TB, 0, s>>>(d, t, counts);
+  else k_net_push<BSR, 0, SPANW, CH><<<blocks, TB, 0, s>>>(d, t, counts);
+}
+
 void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s) {
-  const int blocks = (d.n_pre + TB - 1) / TB;
-  if (d.bsr) {
-    if (seg == 1) k_net_push<true, 1><<<blocks, TB, 0, s>>>(d, t, counts);
-    else if (seg == 2) k_net_push<true, 2><<<blocks, TB, 0, s>>>(d, t, counts);
-    else k_net_push<true, 0><<<blocks, TB, 0, s>>>(d, t, counts);
-  } else {
-    if (seg == 1) k_net_push<false, 1><<<blocks, TB, 0, s>>>(d, t, counts);
-    else if (seg == 2) k_net_push<false, 2><<<blocks, TB, 0, s>>>(d, t, counts);
-    else k_net_push<false, 0><<<blocks, TB, 0, s>>>(d, t, counts);
+  if (d.bsr) return push_seg<true, 8, 16>(d, t, counts, seg, s);
+  if (d.push_span_words == 64) {
+    if (d.push_chunk == 8) return push_seg<false, 64, 8>(d, t, counts, seg, s);
+    return push_seg<false, 64, 16>(d, t, counts, seg, s);
   }
+  if (d.push_chunk == 8) return push_seg<false, 8, 8>(d, t, counts, seg, s);
+  return push_seg<false, 8, 16>(d, t, counts, seg, s);
 }
 
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s) { k_set_tick<<<1, 1, 0, s>>>(t_dev, value); }

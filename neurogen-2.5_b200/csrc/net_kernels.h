@@ -36,6 +36,8 @@ struct NetDev {
   int2 *ring;
   uint32_t *bitmask;            // spike words of the whole network, two buffers (tick parity)
   int bm_stride;                // words per buffer
+  int push_span_words;          // split push: bitmask words a CTA scans (8 or 64)
+  int push_chunk;               // split push: synapses a lane takes a pass (8 or 16)
   // Running counters since creation, three per 256-neuron group: [g][0]
   // spikes of held group g (membrane kernel), [g][1] events pushed from
   // presynaptic group g by the delay-1 (or whole-row) push, [g][2] by the

@@ -291,3 +291,29 @@ def test_resident_barrier_wait_runs_out_cleanly(tmp_path):
     assert out.returncode == 0, out.stderr[-3000:]
     assert 'raised:' in out.stdout and 'timed out' in out.stdout
     assert 'after:' in out.stdout and int(out.stdout.split('after:')[1]) > 0
+
+
+def test_split_push_shapes_agree_at_one_million_neurons(monkeypatch):
+    """The split push's CTA span (8 or 64 bitmask words) and per-lane chunk (8 or 16 synapses)
+    change only the work layout: a 1,048,576-neuron network gives the same spikes, counts and
+    state for every combination."""
+    cfg = default_config(n=1048576, n_exc=838860, topology='fixed_fanin', fanin=24, weight_kind='halfnormal_f16',
+                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.02, seed=9, launch='split')
+    results = []
+    for span in ('8', '64'):
+        for chunk in ('8', '16'):
+            monkeypatch.setenv('NEUROGEN_PUSH_SPAN', span)
+            monkeypatch.setenv('NEUROGEN_PUSH_CHUNK', chunk)
+            net = Network(cfg)
+            s, c = net.run(12)
+            net.run_device(70)
+            results.append((s, c, net.get_state(), net.stats()))
+            del net
+    s0, c0, st0, t0 = results[0]
+    assert c0[:, 1].sum() > 0
+    for s, c, st, tot in results[1:]:
+        np.testing.assert_array_equal(s, s0)
+        np.testing.assert_array_equal(c, c0)
+        for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring'):
+            assert np.array_equal(st[k], st0[k]), k
+        assert tot == t0
