@@ -200,6 +200,7 @@ int ng_pool_step(void *p, const int *tokens, float *logits, float *hidden, float
     if (activity)
       NGB_CUDA(cudaMemcpyAsync(activity, pool.act.as<float>(), size_t(B) * 4, cudaMemcpyDeviceToHost, st));
     NGB_CUDA(cudaStreamSynchronize(st));
+    m.check_device_errors();
   });
 }
 

@@ -179,10 +179,19 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   head_wr = upload(head_w, size_t(kVocab) * w);
   head_b = upload(take(kVocab), kVocab);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  NGB_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&readout_err), sizeof(int), cudaHostAllocMapped));
+  *readout_err = 0;
+  NGB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void **>(&readout_err_dev), readout_err, 0));
 }
 
 DeviceModel::~DeviceModel() {
   if (stream) cudaStreamDestroy(stream);
+  if (readout_err) cudaFreeHost(readout_err);
+}
+
+void DeviceModel::check_device_errors() const {
+  if (readout_err && *reinterpret_cast<volatile int *>(readout_err))
+    throw std::runtime_error("Readout kernel timed out waiting for its tensor-core pipeline");
 }
 
 void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs, bool first_idle,
@@ -297,6 +306,11 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
     }
   }
   if (d_logits) {
+    // Readout on the tensor cores when there is more than one session;
+    // the sequential SIMT projection otherwise.
+    const ReadoutArgs ra{sc.h, d.w, head_wr.as<float>(), head_b.as<float>(), d_logits, kVocab,
+                         B, d.w, kVocab, readout_err_dev};
+    if (!launch_readout_tc(ra, st)) {
     ProjArgs ha{};
     ha.wp = head_wp.as<float>();
     ha.wr = head_wr.as<float>();
@@ -309,6 +323,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
     ha.K = d.w;
     ha.B = B;
     launch_projection(ha, st);
+    }
   }
   if (d_hidden)
     NGB_CUDA(cudaMemcpyAsync(d_hidden, sc.h, size_t(B) * d.w * 4, cudaMemcpyDeviceToDevice, st));
@@ -412,6 +427,7 @@ void NeuralEngine::step_batch(const int *tokens, int batch, const float *state, 
   if (activity)
     NGB_CUDA(cudaMemcpyAsync(activity, sc.act.as<float>(), size_t(batch) * 4, cudaMemcpyDeviceToHost, st));
   NGB_CUDA(cudaStreamSynchronize(st));
+  m.check_device_errors();
 }
 
 void NeuralEngine::advance_batch(const float *inputs, int batch, const float *state, bool idle,
@@ -436,6 +452,7 @@ void NeuralEngine::advance_batch(const float *inputs, int batch, const float *st
   if (activity)
     NGB_CUDA(cudaMemcpyAsync(activity, sc.act.as<float>(), size_t(batch) * 4, cudaMemcpyDeviceToHost, st));
   NGB_CUDA(cudaStreamSynchronize(st));
+  m.check_device_errors();
 }
 
 Vector NeuralEngine::step(int token, std::vector<ColumnState> &state, Vector &hidden, float &activity) {

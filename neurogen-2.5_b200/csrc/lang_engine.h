@@ -79,6 +79,11 @@ public:
   DeviceBuffer emb, head_wp, head_b, head_wr;
   std::vector<RegionWeights> regions;
   Scratch host_scratch; // used by the host-buffer entry points (under the engine mutex)
+  // Error word of the tensor-core readout (pinned, mapped into the device):
+  // nonzero after one of its bounded waits timed out.
+  int *readout_err = nullptr, *readout_err_dev = nullptr;
+  // Throws when a kernel reported an error; call after synchronising.
+  void check_device_errors() const;
 };
 
 } // namespace ngb

@@ -743,6 +743,7 @@ __global__ void k_activity(const int *counts, int A, int R, int n, int T, float 
 } // namespace
 
 void configure_lang_kernels() {
+  configure_readout_tc();
   configure_ticks_cluster<4, 1>();
   configure_ticks_cluster<4, 2>();
   configure_ticks_cluster<4, 4>();
@@ -783,6 +784,7 @@ void preload_lang_kernels() {
                            (const void *)k_norm,
                            (const void *)k_activity};
   for (const void *k : kernels) cudaFuncGetAttributes(&fa, k);
+  cudaFuncGetAttributes(&fa, readout_tc_kernel());
 }
 
 void launch_projections(const ProjBatch &pb, cudaStream_t s) {

@@ -41,6 +41,31 @@ struct ProjBatch {
   int count;
 };
 void launch_projections(const ProjBatch &pb, cudaStream_t s);
+
+// Token readout y[b][v] = bias[v] + sum_k h[b][k] * w[v][k] on the tcgen05
+// tensor cores (readout_tc.cu): split-tf32 operands, fp32 TMEM accumulators.
+// Deterministic and within a few 1e-6 of the logit vector's scale of the
+// sequential fp32 sum, but not bit-identical to it.  *err (device-visible,
+// may be null) is set to 1 when a bounded wait in the kernel timed out.
+struct ReadoutArgs {
+  const float *h; // [B] rows of K, row stride ldh
+  long ldh;
+  const float *w;    // [V][K] row-major
+  const float *bias; // [V] or null
+  float *y;          // [B] rows of V, row stride ldy
+  long ldy;
+  int B, K, V;
+  int *err;
+};
+// False when NEUROGEN_READOUT=simt is set (the sequential SIMT projection is
+// then used at every batch size).
+bool readout_tc_enabled();
+// Shapes the kernel takes: B >= 2, K a multiple of 4, 16-byte aligned rows.
+bool readout_tc_ok(const ReadoutArgs &a);
+// Launches when readout_tc_ok(a); returns false (nothing launched) otherwise.
+bool launch_readout_tc(const ReadoutArgs &a, cudaStream_t s);
+void configure_readout_tc();
+const void *readout_tc_kernel();
 // Per-device kernel attributes (dynamic shared memory); call once per device
 // before launching, outside any stream capture.
 void configure_lang_kernels();

@@ -3,6 +3,11 @@
 Bars: spike indices identical for the first 100 ticks; state within 1e-5
 relative; logits within 1e-4 relative.  The engine reproduces the reference's fp32 operation
 order, so most outputs are bit-identical; the measured counts are printed for the record.
+The exception is the token readout of two or more sessions, which runs on the tensor cores
+(split-tf32): its logits are held to 1e-4 relative elementwise with an absolute floor of 1e-4
+of the logit vector's largest magnitude (a logit near zero is a difference of much larger
+terms, so no fp32 method other than the reference's own operation order gets it to 1e-4 of
+itself).  The readout does not feed the state, which stays exact.
 """
 import threading
 
@@ -17,6 +22,11 @@ pytestmark = pytest.mark.gpu
 SMALL = LanguageConfig(columns=3, width=17, regions=2, ticks=3, idle_steps=1, speech_width=16, mel_bins=8)
 STATE_RTOL, STATE_ATOL = 1e-5, 1e-6
 LOGIT_RTOL, LOGIT_ATOL = 1e-4, 1e-6
+
+
+def assert_logits_close(got, want):
+    """Tensor-core readout bar: 1e-4 relative, floor 1e-4 of the vector's largest logit."""
+    np.testing.assert_allclose(got, want, rtol=LOGIT_RTOL, atol=LOGIT_RTOL * float(np.abs(want).max()))
 
 
 def fields(cfg, state):
@@ -63,7 +73,9 @@ def test_small_config_tokens_and_idle_vs_reference(golden_lang):
     print(f'bit-identical token steps: {exact}/{total}')
 
 
-def test_batch_rows_equal_single_session_runs():
+def test_batch_rows_equal_single_session_runs(monkeypatch):
+    """With the SIMT readout every output of a batched step has the bits of a batch-1 step."""
+    monkeypatch.setenv('NEUROGEN_READOUT', 'simt')
     cfg = LanguageConfig(columns=4, width=40, regions=2, ticks=2, idle_steps=1)
     w = init_packed_weights(cfg, seed=3)
     eng = NativeEngine(cfg, w)
@@ -148,7 +160,7 @@ def test_batched_sessions_vs_reference():
         lb, sb, ab, hb = eng.step_batch(toks[t], sb)
         for b in range(B):
             lr, sr[b], ar, hr = ref.step(int(toks[t, b]), sr[b])
-            np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+            assert_logits_close(lb[b], lr)
             assert_state_close(cfg, sb[b], sr[b])
 
 
@@ -252,7 +264,7 @@ for t in range(3):
         assert np.array_equal(l1[0], lb[b]) and np.array_equal(s1[0], sb[b]), (t, b)
 print('ok')
 """
-    env = dict(os.environ, **{var: tile})
+    env = dict(os.environ, **{var: tile, 'NEUROGEN_READOUT': 'simt'})
     out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0 and 'ok' in out.stdout, out.stderr[-2000:]
 
@@ -279,7 +291,10 @@ def test_tick_paths_match_reference(columns, ticks, batch):
         lb, sb, ab, hb = eng.step_batch(toks, sb)
         for b in range(batch):
             lr, sr[b], ar, hr = ref.step(int(toks[b]), sr[b])
-            np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
+            if batch > 1:
+                assert_logits_close(lb[b], lr)
+            else:
+                np.testing.assert_allclose(lb[b], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL)
             assert_state_close(cfg, sb[b], sr[b])
 
 
@@ -309,3 +324,63 @@ def test_session_pool_save_load_roundtrip(tmp_path):
         lb = b.step(np.array([toks[2], 7, 9]))
         assert np.array_equal(la[2], lb[0])
     assert np.array_equal(a.states()[2], b.states()[0])
+
+
+def head_weights(cfg, w):
+    """Head Linear(width, 264) at the end of the packed weight vector: weight [264][w], bias."""
+    n = 264 * cfg.width + 264
+    tail = w[-n:]
+    return tail[:264 * cfg.width].reshape(264, cfg.width).astype(np.float64), tail[264 * cfg.width:].astype(np.float64)
+
+
+@pytest.mark.parametrize('B', [2, 37, 128, 130, 256])
+def test_tensor_core_readout_bc250(B, monkeypatch):
+    """The tcgen05 readout of B sessions (BC-250, K=768: 24 k chunks in 4 segments) against the
+    float64 product of the same hidden states, against the sequential SIMT readout, and the
+    state bit-identical between the two readouts (the readout feeds nothing back)."""
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng = NativeEngine(cfg, w)
+    W, bias = head_weights(cfg, w)
+    rng = np.random.default_rng(B)
+    s0 = np.zeros((B, eng.state_size), np.float32)
+    for _ in range(2):   # move off the zero state
+        _, s0, _, _ = eng.step_batch(rng.integers(0, 264, B), s0)
+    toks = rng.integers(0, 264, B)
+    lt, st, at, ht = eng.step_batch(toks, s0)
+    exact = ht.astype(np.float64) @ W.T + bias
+    scale = np.abs(exact).max(axis=1, keepdims=True)
+    err = np.abs(lt - exact) / scale
+    print(f'B={B}: max |tc - f64| / row scale = {err.max():.2e}')
+    assert err.max() < 2e-5
+    monkeypatch.setenv('NEUROGEN_READOUT', 'simt')
+    ls, ss, as_, hs = eng.step_batch(toks, s0)
+    assert np.array_equal(ss, st) and np.array_equal(hs, ht) and np.array_equal(as_, at)
+    assert_logits_close(lt, ls)
+    assert not np.array_equal(lt, ls)   # the tensor-core path did run
+
+
+def test_tensor_core_readout_ragged_k_and_fallback(monkeypatch):
+    """K=40 (a partial k chunk, fewer chunks than segments) on the tensor cores; K=17 (rows not
+    16-byte aligned) falls back to the SIMT readout, bit-identical to batch 1."""
+    for width, tc in ((40, True), (17, False)):
+        cfg = LanguageConfig(columns=2, width=width, regions=2, ticks=2, idle_steps=1)
+        w = init_packed_weights(cfg, seed=width)
+        eng = NativeEngine(cfg, w)
+        W, bias = head_weights(cfg, w)
+        B = 9
+        rng = np.random.default_rng(0)
+        sb = np.zeros((B, eng.state_size), np.float32)
+        for _ in range(3):
+            lb, sb, _, hb = eng.step_batch(rng.integers(0, 264, B), sb)
+        exact = hb.astype(np.float64) @ W.T + bias
+        err = np.abs(lb - exact) / np.abs(exact).max(axis=1, keepdims=True)
+        assert err.max() < 2e-5
+        l1, _, _, _ = eng.step_batch(np.array([5]), sb[:1])
+        monkeypatch.setenv('NEUROGEN_READOUT', 'simt')
+        l1s, _, _, _ = eng.step_batch(np.array([5]), sb[:1])
+        lbs, _, _, _ = eng.step_batch(np.full(B, 5), sb)
+        monkeypatch.delenv('NEUROGEN_READOUT')
+        lbt, _, _, _ = eng.step_batch(np.full(B, 5), sb)
+        assert np.array_equal(l1, l1s) and np.array_equal(lbs[0], l1s[0])
+        assert np.array_equal(lbt, lbs) != tc
