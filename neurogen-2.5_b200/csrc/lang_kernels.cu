@@ -448,6 +448,213 @@ __global__ void __launch_bounds__(rm_threads<RB, BS>()) k_gemm_rm(ProjBatch pb) 
 
 template <int RB, int BS> size_t gemm_rm_smem() { return sizeof(float) * RM_STAGES * rm_stage_floats<RB, BS>(); }
 
+// ---------------------------------------------------------------------------
+// Projection, register-tiled (many sessions): 64 threads a CTA as an 8 x 8
+// grid; thread (rt, st) owns TR rows x TS sessions, i.e. TR/2 x TS chains of
+// row pairs (one add.rn.f32x2 each).  Per k a thread loads its TR weights
+// (one shared-memory vector load) and TS inputs and issues TR*TS scalar
+// __fmul_rn and TR*TS/2 packed adds, so the fp32 pipe, not shared-memory
+// latency, sets the pace.  Weights stream from the 32-row panel layout by
+// cp.async (RB = 8*TR rows of one panel are contiguous per k); the inputs are
+// read 16 bytes at a time by the CTA's threads and stored transposed,
+// [k][session], one chunk ahead of use.  Every output is still one
+// sequential chain bias + w0*x0 + w1*x1 + ... : bits identical to every other
+// projection kernel.
+// ---------------------------------------------------------------------------
+constexpr int RG_KC = 32, RG_STAGES = 4, RG_THREADS = 64, RG_AHEAD = 6;
+template <int TR, int TS> __host__ __device__ constexpr int rg_rows() { return 8 * TR; }
+template <int TR, int TS> __host__ __device__ constexpr int rg_sessions() { return 8 * TS; }
+// Input tile row stride: sessions + 4 floats, so the transposing stores of the
+// two k groups a warp writes land in different banks (and rows stay 16-byte aligned).
+template <int TR, int TS> __host__ __device__ constexpr int rg_xld() { return 8 * TS + 4; }
+template <int TR, int TS> __host__ __device__ constexpr int rg_stage_floats() {
+  return RG_KC * (rg_rows<TR, TS>() + rg_xld<TR, TS>());
+}
+template <int TR, int TS> size_t gemm_rg_smem() { return sizeof(float) * RG_STAGES * rg_stage_floats<TR, TS>(); }
+
+template <int N> __device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
+  if constexpr (N == 4) {
+    const float4 t = *reinterpret_cast<const float4 *>(p);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else if constexpr (N == 2) {
+    const float2 t = *reinterpret_cast<const float2 *>(p);
+    v[0] = t.x, v[1] = t.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = p[i];
+  }
+}
+
+template <int TR, int TS>
+__global__ void __launch_bounds__(RG_THREADS) k_gemm_rg(ProjBatch pb) {
+  constexpr int RB = rg_rows<TR, TS>(), BS = rg_sessions<TR, TS>(), XLD = rg_xld<TR, TS>();
+  constexpr int STAGE = rg_stage_floats<TR, TS>();
+  constexpr int WPIECES = RG_KC * RB / 4 / RG_THREADS; // 16-byte weight copies a thread, per chunk
+  constexpr int XPIECES = BS * RG_KC / 4 / RG_THREADS; // 16-byte input loads a thread, per chunk
+  static_assert(TR % 2 == 0 && 32 % RB == 0 && WPIECES >= 1 && XPIECES >= 1, "tile");
+  extern __shared__ __align__(16) float sm[];
+  const ProjArgs &a = pb.a[blockIdx.z];
+  const int m0 = blockIdx.x * RB, b0 = blockIdx.y * BS;
+  if (m0 >= a.M || b0 >= a.B) return;
+  const int tid = threadIdx.x, rt = tid % 8, st = tid / 8;
+  const int nch = (a.K + RG_KC - 1) / RG_KC;
+  // Weights: panel rows m0 .. m0+RB-1 are RB contiguous floats for each k
+  // (rows past M are the panel's zero padding).
+  const float *wq = a.wp + (size_t)(m0 >> 5) * a.K * 32 + (m0 & 31);
+  auto issue_w = [&](int ch) {
+    if (ch < nch) {
+      const int k0 = ch * RG_KC, kc = min(RG_KC, a.K - k0);
+      float *ws = sm + (ch % RG_STAGES) * STAGE;
+#pragma unroll
+      for (int j = 0; j < WPIECES; ++j) {
+        const int i = tid + j * RG_THREADS, k = i / (RB / 4), q = i % (RB / 4);
+        if (k < kc) cp_async16(ws + k * RB + q * 4, wq + (size_t)(k0 + k) * 32 + q * 4);
+      }
+    }
+    cp_async_commit();
+  };
+  // Inputs: piece i = (session i % BS, k quad i / BS); rows past B and k past
+  // K read as zero.
+  const float *xrow[XPIECES];
+  int xs_sess[XPIECES], xs_kq[XPIECES];
+#pragma unroll
+  for (int j = 0; j < XPIECES; ++j) {
+    const int i = tid + j * RG_THREADS, sidx = i % BS, b = b0 + sidx;
+    xs_sess[j] = sidx;
+    xs_kq[j] = i / BS;
+    xrow[j] = b < a.B ? a.x + (long)(a.xidx ? a.xidx[b] : b) * a.ldx : nullptr;
+  }
+  float4 xr[XPIECES];
+  auto load_x = [&](int ch) {
+    const int k0 = ch * RG_KC;
+#pragma unroll
+    for (int j = 0; j < XPIECES; ++j) {
+      const int k = k0 + 4 * xs_kq[j];
+      xr[j] = (xrow[j] && k < a.K) ? *reinterpret_cast<const float4 *>(xrow[j] + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store_x = [&](int ch) {
+    float *xs = sm + (ch % RG_STAGES) * STAGE + RG_KC * RB;
+#pragma unroll
+    for (int j = 0; j < XPIECES; ++j) {
+      float *d = xs + 4 * xs_kq[j] * XLD + xs_sess[j];
+      d[0] = xr[j].x;
+      d[XLD] = xr[j].y;
+      d[2 * XLD] = xr[j].z;
+      d[3 * XLD] = xr[j].w;
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < RG_STAGES - 1; ++s) issue_w(s);
+  load_x(0);
+  store_x(0);
+  if (nch > 1) load_x(1);
+
+  // acc[p][s]: rows (m0 + TR*rt + 2p, +1) of session b0 + TS*st + s.
+  f32x2 acc[TR / 2][TS];
+#pragma unroll
+  for (int p = 0; p < TR / 2; ++p) {
+    const int m = m0 + TR * rt + 2 * p;
+    const float lo = (a.bias && m < a.M) ? a.bias[m] : 0.f, hi = (a.bias && m + 1 < a.M) ? a.bias[m + 1] : 0.f;
+#pragma unroll
+    for (int s = 0; s < TS; ++s) acc[p][s] = pack2(lo, hi);
+  }
+  for (int ch = 0; ch < nch; ++ch) {
+    cp_async_wait<RG_STAGES - 2>();
+    __syncthreads();
+    issue_w(ch + RG_STAGES - 1);
+    if (ch + 1 < nch) store_x(ch + 1);
+    if (ch + 2 < nch) load_x(ch + 2);
+    const float *ws = sm + (ch % RG_STAGES) * STAGE + TR * rt;
+    const float *xs = sm + (ch % RG_STAGES) * STAGE + RG_KC * RB + TS * st;
+    auto fma_step = [&](const float (&w)[TR], const float (&x)[TS]) {
+#pragma unroll
+      for (int p = 0; p < TR / 2; ++p)
+#pragma unroll
+        for (int s = 0; s < TS; ++s)
+          acc[p][s] = add2(acc[p][s], pack2(__fmul_rn(w[2 * p], x[s]), __fmul_rn(w[2 * p + 1], x[s])));
+    };
+    const int kc = min(RG_KC, a.K - ch * RG_KC);
+    if (kc == RG_KC) {
+      // Three-stage software pipeline over k: operands of step k + RG_AHEAD
+      // are loaded and the products of step k + 1 formed while step k's
+      // products are added, so neither shared-memory nor multiply latency
+      // sits between two adds of a chain.
+      float w[RG_AHEAD][TR], x[RG_AHEAD][TS];
+      f32x2 pr[TR / 2][TS];
+#pragma unroll
+      for (int d = 0; d < RG_AHEAD; ++d) {
+        lds_vec<TR>(ws + d * RB, w[d]);
+        lds_vec<TS>(xs + d * XLD, x[d]);
+      }
+      auto products = [&](const float (&wv)[TR], const float (&xv)[TS]) {
+#pragma unroll
+        for (int p = 0; p < TR / 2; ++p)
+#pragma unroll
+          for (int s = 0; s < TS; ++s) pr[p][s] = pack2(__fmul_rn(wv[2 * p], xv[s]), __fmul_rn(wv[2 * p + 1], xv[s]));
+      };
+      products(w[0], x[0]);
+#pragma unroll
+      for (int k = 0; k < RG_KC; ++k) {
+        f32x2 cur[TR / 2][TS];
+#pragma unroll
+        for (int p = 0; p < TR / 2; ++p)
+#pragma unroll
+          for (int s = 0; s < TS; ++s) cur[p][s] = pr[p][s];
+        if (k + RG_AHEAD < RG_KC) {
+          lds_vec<TR>(ws + (k + RG_AHEAD) * RB, w[k % RG_AHEAD]);
+          lds_vec<TS>(xs + (k + RG_AHEAD) * XLD, x[k % RG_AHEAD]);
+        }
+        if (k + 1 < RG_KC) products(w[(k + 1) % RG_AHEAD], x[(k + 1) % RG_AHEAD]);
+#pragma unroll
+        for (int p = 0; p < TR / 2; ++p)
+#pragma unroll
+          for (int s = 0; s < TS; ++s) acc[p][s] = add2(acc[p][s], cur[p][s]);
+      }
+    } else {
+      for (int k = 0; k < kc; ++k) {
+        float w[TR], x[TS];
+        lds_vec<TR>(ws + k * RB, w);
+        lds_vec<TS>(xs + k * XLD, x);
+        fma_step(w, x);
+      }
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < TR / 2; ++p)
+#pragma unroll
+    for (int s = 0; s < TS; ++s) {
+      float r[2];
+      unpack2(acc[p][s], r[0], r[1]);
+      const int b = b0 + TS * st + s;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int m = m0 + TR * rt + 2 * p + i;
+        if (m < a.M && b < a.B) {
+          float v = r[i];
+          if (a.addv) v = __fadd_rn(v, __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + m]));
+          a.y[(long)b * a.ldy + m] = v;
+        }
+      }
+    }
+}
+
+template <int TR, int TS> void run_gemm_rg(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
+  dim3 grid((max_m + rg_rows<TR, TS>() - 1) / rg_rows<TR, TS>(),
+            (max_b + rg_sessions<TR, TS>() - 1) / rg_sessions<TR, TS>(), pb.count);
+  k_gemm_rg<TR, TS><<<grid, RG_THREADS, gemm_rg_smem<TR, TS>(), s>>>(pb);
+}
+
+// Register-tiled operands usable: K, ldx and the input base 16-byte aligned
+// (the weights come from the panel layout, always aligned).
+bool rg_ok(const ProjBatch &pb) {
+  for (int z = 0; z < pb.count; ++z) {
+    const ProjArgs &a = pb.a[z];
+    if (a.K % 4 || a.ldx % 4 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return false;
+  }
+  return true;
+}
+
 template <int RB, int BS> void run_gemm_rm(const ProjBatch &pb, int max_m, int max_b, cudaStream_t s) {
   dim3 grid((max_m + RB - 1) / RB, (max_b + BS - 1) / BS, pb.count);
   k_gemm_rm<RB, BS><<<grid, rm_threads<RB, BS>(), gemm_rm_smem<RB, BS>(), s>>>(pb);
@@ -753,6 +960,12 @@ void configure_lang_kernels() {
   configure_gemm<16, 2>();
   configure_gemm<32, 4>();
   configure_gemm<64, 4>();
+  cudaFuncSetAttribute(k_gemm_rg<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<2, 2>());
+  cudaFuncSetAttribute(k_gemm_rg<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<4, 2>());
+  cudaFuncSetAttribute(k_gemm_rg<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<2, 4>());
+  cudaFuncSetAttribute(k_gemm_rg<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<4, 4>());
+  cudaFuncSetAttribute(k_gemm_rg<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<4, 3>());
+  cudaFuncSetAttribute(k_gemm_rg<2, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rg_smem<2, 3>());
   cudaFuncSetAttribute(k_gemm_rm<16, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rm_smem<16, 8>());
   cudaFuncSetAttribute(k_gemm_rm<32, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_rm_smem<32, 8>());
   cudaFuncSetAttribute(k_gemm_sb<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_sb_smem<8>());
@@ -765,6 +978,12 @@ void configure_lang_kernels() {
 void preload_lang_kernels() {
   cudaFuncAttributes fa;
   const void *kernels[] = {(const void *)k_gemv,
+                           (const void *)k_gemm_rg<2, 2>,
+                           (const void *)k_gemm_rg<4, 2>,
+                           (const void *)k_gemm_rg<2, 4>,
+                           (const void *)k_gemm_rg<4, 4>,
+                           (const void *)k_gemm_rg<4, 3>,
+                           (const void *)k_gemm_rg<2, 3>,
                            (const void *)k_gemm_rm<16, 8>,
                            (const void *)k_gemm_rm<32, 8>,
                            (const void *)k_gemm_sb<8>,
@@ -822,6 +1041,22 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s) {
     const char *v = std::getenv("NEUROGEN_PROJ_ROWMAJOR");
     return v ? std::atoi(v) : 0;
   }();
+  // NEUROGEN_PROJ_REG = 22 | 42 | 24 | 44 forces the register-tiled kernel
+  // with that many rows and sessions a thread (when its operands qualify).
+  static const int forced_rg = [] {
+    const char *v = std::getenv("NEUROGEN_PROJ_REG");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (forced_rg > 0 && rg_ok(pb)) {
+    switch (forced_rg) {
+    case 42: return run_gemm_rg<4, 2>(pb, max_m, max_b, s);
+    case 24: return run_gemm_rg<2, 4>(pb, max_m, max_b, s);
+    case 44: return run_gemm_rg<4, 4>(pb, max_m, max_b, s);
+    case 43: return run_gemm_rg<4, 3>(pb, max_m, max_b, s);
+    case 23: return run_gemm_rg<2, 3>(pb, max_m, max_b, s);
+    default: return run_gemm_rg<2, 2>(pb, max_m, max_b, s);
+    }
+  }
   if (forced_rm && rm_ok(pb)) {
     if (forced_rm == 32) return run_gemm_rm<32, 8>(pb, max_m, max_b, s);
     return run_gemm_rm<16, 8>(pb, max_m, max_b, s);
@@ -838,6 +1073,20 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s) {
   case 32: return run_gemm<32, 4>(pb, max_m, max_b, s);
   case 64: return run_gemm<64, 4>(pb, max_m, max_b, s);
   default: break;
+  }
+  // Register tiles when they give every SM sub-partition (148 x 4) at least
+  // one warp: 4 rows x 2 sessions a thread, else 2 x 2 (BC-250, 256 sessions:
+  // feedback 4x2, input 2x2, output 4x2; 122 K -> 160 K tokens/s).
+  // NEUROGEN_PROJ_REG=-1 keeps the row-major kernel at every size.
+  if (forced_rg == 0 && rg_ok(pb)) {
+    auto rg_warps = [&](int rows, int sessions) {
+      long w = 0;
+      for (int z = 0; z < pb.count; ++z)
+        w += long((pb.a[z].M + rows - 1) / rows) * ((pb.a[z].B + sessions - 1) / sessions) * (RG_THREADS / 32);
+      return w;
+    };
+    if (rg_warps(rg_rows<4, 2>(), rg_sessions<4, 2>()) >= want) return run_gemm_rg<4, 2>(pb, max_m, max_b, s);
+    if (rg_warps(rg_rows<2, 2>(), rg_sessions<2, 2>()) >= want) return run_gemm_rg<2, 2>(pb, max_m, max_b, s);
   }
   // Row-major operands (the engine's default): 16 rows x 8 sessions a CTA,
   // measured fastest at every batch on BC-250 (32 / 64 / 128 / 256 sessions:

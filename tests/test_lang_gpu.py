@@ -237,7 +237,8 @@ def test_pool_matches_host_batch():
 
 @pytest.mark.parametrize('var,tile', [('NEUROGEN_PROJ_TILE', t) for t in ('8', '16', '32', '64')] +
                          [('NEUROGEN_PROJ_SMALL', t) for t in ('8', '16', '32')] +
-                         [('NEUROGEN_PROJ_ROWMAJOR', t) for t in ('16', '32')])
+                         [('NEUROGEN_PROJ_ROWMAJOR', t) for t in ('16', '32')] +
+                         [('NEUROGEN_PROJ_REG', t) for t in ('22', '42', '24', '44', '43', '23')])
 def test_every_projection_tile_is_bit_identical(var, tile):
     """Each session tile of the batched projection kernels (wide tiles and the small-batch
     kernel) gives the same bits as the batch-1 kernel (one sequential chain per output in every
