@@ -95,6 +95,8 @@ void Scratch::ensure(const LangDims &d, int batch) {
   logits.reset(B * kVocab * 4);
   hidden.reset(B * d.w * 4);
   act.reset(B * 4);
+  h_hi.reset(B * d.w * 4);
+  h_lo.reset(B * d.w * 4);
   capacity = batch;
 }
 
@@ -177,6 +179,18 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   const float *head_w = take(size_t(kVocab) * w);
   head_wp = upload(to_panels(head_w, kVocab, w));
   head_wr = upload(head_w, size_t(kVocab) * w);
+  {
+    std::vector<float> hi(size_t(kVocab) * w), lo(hi.size());
+    for (size_t i = 0; i < hi.size(); ++i) {
+      uint32_t bits;
+      std::memcpy(&bits, head_w + i, 4);
+      bits &= 0xFFFFE000u;
+      std::memcpy(&hi[i], &bits, 4);
+      lo[i] = head_w[i] - hi[i]; // exact in fp32
+    }
+    head_hi = upload(hi);
+    head_lo = upload(lo);
+  }
   head_b = upload(take(kVocab), kVocab);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   NGB_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&readout_err), sizeof(int), cudaHostAllocMapped));
@@ -201,6 +215,12 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
   const int A = advances;
   NGB_CUDA(cudaMemsetAsync(sc.cnt, 0, size_t(B) * A * d.R * sizeof(int), st));
   const int Min = d.c * d.n_in, Mfb = d.c * d.n_fb, Kout = d.c * d.n_out * 2;
+  // Readout on the tensor cores when there is more than one session and the
+  // split hidden state has somewhere to go; the sequential SIMT projection
+  // otherwise.  The last LayerNorm writes the split.
+  const ReadoutArgs ra{sc.h_hi, sc.h_lo, d.w, head_hi.as<float>(), head_lo.as<float>(), head_b.as<float>(),
+                       d_logits, kVocab, B, d.w, kVocab, readout_err_dev};
+  const bool tc_readout = d_logits && readout_tc_ok(ra);
   for (int adv = 0; adv < A; ++adv) {
     const bool idle = adv > 0 || first_idle;
     // Feedback projections of every region read only that region's memory,
@@ -302,15 +322,15 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       na.decay = g.decay.as<float>();
       na.w = d.w;
       na.B = B;
+      if (tc_readout && adv == A - 1 && r == d.R - 1) {
+        na.h_hi = sc.h_hi;
+        na.h_lo = sc.h_lo;
+      }
       launch_norm(na, st);
     }
   }
   if (d_logits) {
-    // Readout on the tensor cores when there is more than one session;
-    // the sequential SIMT projection otherwise.
-    const ReadoutArgs ra{sc.h, d.w, head_wr.as<float>(), head_b.as<float>(), d_logits, kVocab,
-                         B, d.w, kVocab, readout_err_dev};
-    if (!launch_readout_tc(ra, st)) {
+    if (!tc_readout || !launch_readout_tc(ra, st)) {
     ProjArgs ha{};
     ha.wp = head_wp.as<float>();
     ha.wr = head_wr.as<float>();

@@ -36,16 +36,17 @@ struct RegionWeights {
 struct ScratchView {
   float *h, *hraw, *vin, *fb, *tr, *feat;
   int *cnt;
+  float *h_hi = nullptr, *h_lo = nullptr; // tf32 split of h for the tensor-core readout, or null
 };
 
 // Per-call device workspace for `capacity` sessions.
 struct Scratch {
   int capacity = 0;
-  DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act;
+  DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act, h_hi, h_lo;
   void ensure(const LangDims &d, int batch);
   ScratchView view() const {
     return {h.as<float>(), hraw.as<float>(), vin.as<float>(), fb.as<float>(),
-            tr.as<float>(), feat.as<float>(), cnt.as<int>()};
+            tr.as<float>(), feat.as<float>(), cnt.as<int>(), h_hi.as<float>(), h_lo.as<float>()};
   }
 };
 
@@ -77,6 +78,7 @@ public:
   cudaStream_t stream = nullptr;
   UnitTables tables;
   DeviceBuffer emb, head_wp, head_b, head_wr;
+  DeviceBuffer head_hi, head_lo; // tf32 split of head_wr for the tensor-core readout
   std::vector<RegionWeights> regions;
   Scratch host_scratch; // used by the host-buffer entry points (under the engine mutex)
   // Error word of the tensor-core readout (pinned, mapped into the device):

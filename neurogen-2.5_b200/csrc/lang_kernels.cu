@@ -928,6 +928,11 @@ __global__ void __launch_bounds__(LN_T) k_norm(NormArgs a) {
   for (int i = threadIdx.x; i < a.w; i += LN_T) {
     const float y = (hr[i] - mf) * inv * a.norm_w[i] + a.norm_b[i];
     h[i] = y;
+    if (a.h_hi) {
+      const float hi = __uint_as_float(__float_as_uint(y) & 0xFFFFE000u);
+      a.h_hi[(long)b * a.h_ld + i] = hi;
+      a.h_lo[(long)b * a.h_ld + i] = __fsub_rn(y, hi);
+    }
     const float d = a.decay[i];
     mem[i] = d * mem[i] + (1 - d) * y;
   }

@@ -44,14 +44,16 @@ void launch_projections(const ProjBatch &pb, cudaStream_t s);
 
 // Token readout y[b][v] = bias[v] + sum_k h[b][k] * w[v][k] on the tcgen05
 // tensor cores (readout_tc.cu): split-tf32 operands, fp32 TMEM accumulators.
-// Deterministic and within a few 1e-6 of the logit vector's scale of the
-// sequential fp32 sum, but not bit-identical to it.  *err (device-visible,
-// may be null) is set to 1 when a bounded wait in the kernel timed out.
+// Each operand comes as hi = x with the low 13 mantissa bits cleared and
+// lo = x - hi (tf32_split / k_norm's split output).  Deterministic and within
+// a few 1e-6 of the logit vector's scale of the sequential fp32 sum, but not
+// bit-identical to it.  *err (device-visible, may be null) is set to 1 when a
+// bounded wait in the kernel timed out.
 struct ReadoutArgs {
-  const float *h; // [B] rows of K, row stride ldh
+  const float *h_hi, *h_lo; // [B] rows of K, row stride ldh
   long ldh;
-  const float *w;    // [V][K] row-major
-  const float *bias; // [V] or null
+  const float *w_hi, *w_lo; // [V][K] row-major
+  const float *bias;        // [V] or null
   float *y;          // [B] rows of V, row stride ldy
   long ldy;
   int B, K, V;
@@ -110,6 +112,8 @@ struct NormArgs {
   long hraw_ld;
   float *h;
   long h_ld;
+  float *h_hi, *h_lo; // optional tf32 split of h (same row stride): hi = h with the low
+                      // 13 mantissa bits cleared, lo = h - hi; null to skip
   float *mem;
   long mem_ld;
   const float *norm_w, *norm_b, *decay;

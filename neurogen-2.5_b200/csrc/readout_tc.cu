@@ -5,41 +5,48 @@
 // src/native/engine/NeuralEngine.cpp as a sequential fp32 dot product).
 //
 // The tensor cores read fp32 operands as tf32 (10 explicit mantissa bits), so
-// every operand x is split as hi = x with the low 13 mantissa bits cleared
-// (exactly a tf32 value) and lo = x - hi (exact in fp32, read as tf32), and
+// every operand x comes split as hi = x with the low 13 mantissa bits cleared
+// (exactly a tf32 value) and lo = x - hi (exact in fp32, read as tf32): the
+// head weights once at model load, the hidden state by the LayerNorm kernel
+// that produces it.  Then
 //   h.W ~= h_hi.W_hi + (h_lo.W_hi + h_hi.W_lo)
 // with the small terms in their own TMEM accumulator.  The k range is split
-// into up to kSegs segments with separate accumulators, summed in fp32 in the
-// epilogue (bias, main segments, then correction segments, a fixed order), so
-// each accumulator takes few tensor-core additions.  The result is within a
-// few 1e-6 of the vector scale of the sequential fp32 sum; it is deterministic
-// but not bit-identical to it (the SIMT projection, k_gemm_rm / k_gemv, is).
+// into up to kSegs segments, one CTA of a kSegs-CTA cluster each; each
+// segment's main + correction sum, then the segments' sums, are added in fp32
+// in a fixed order, so each accumulator takes few tensor-core additions.  The result is
+// within a few 1e-6 of the vector scale of the sequential fp32 sum; it is
+// deterministic but not bit-identical to it (the SIMT projection is).
 //
 // CTA: 128 sessions (TMEM lanes) x 32 vocabulary rows (TMEM columns), 128
-// threads.  Per 32-wide k chunk, thread 0 loads the fp32 tiles of h and W by
-// TMA (SWIZZLE_128B, kRaw stages deep); all threads split them element by
-// element into hi / lo operand tiles of the same swizzled K-major layout
-// (kOps stages); thread 0 issues the 12 MMAs of the chunk (4 k-steps x 3
-// terms, M=128 N=32 K=8) and commits them to the stage's mbarrier.  Every
-// mbarrier wait is bounded: on a timeout the kernel sets *err, stops issuing,
-// waits (bounded) for work in flight, frees its TMEM and returns.
+// threads.  Thread 0 streams the segment's 32-wide k chunks by TMA
+// (SWIZZLE_128B, kStages deep; h hi / lo and W hi / lo per chunk) and issues
+// the 12 MMAs of each chunk (4 k-steps x 3 terms, M=128 N=32 K=8), committing
+// them to the stage's mbarrier before the stage is refilled.  Each segment
+// leaves its sums in its shared memory; after a cluster barrier every CTA adds
+// up one slice of the rows over all segments (distributed shared memory) and
+// writes those logits.
+// Every mbarrier wait is bounded: on a timeout the kernel sets *err, stops
+// issuing, waits (bounded) for work in flight, frees its TMEM and returns.
 #include "lang_kernels.h"
 
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cstdlib>
 #include <cstring>
 
 namespace ngb {
 namespace {
+namespace cg = cooperative_groups;
 
 constexpr int kBM = 128, kBN = 32, kKC = 32;   // sessions, vocab rows, k per chunk
-constexpr int kRaw = 4, kOps = 2, kSegs = 4;   // raw / operand stages, k segments
+constexpr int kStages = 4, kSegs = 6;          // pipeline stages, k segments (cluster size: 3 clusters fit a GPC)
 constexpr int kThreads = 128;
-constexpr int kTmemCols = 256;                 // kSegs main + kSegs correction accumulators of kBN
+constexpr int kTmemCols = 64;                  // main and correction accumulators of kBN columns
 constexpr uint32_t kTileA = kBM * kKC * 4, kTileB = kBN * kKC * 4; // 16 KB, 4 KB
-constexpr uint32_t kRawBytes = kTileA + kTileB;                    // one raw stage
-constexpr uint32_t kOpBytes = 2 * (kTileA + kTileB);               // hi + lo of both
-constexpr size_t kSmemBytes = 1024 + kRaw * kRawBytes + kOps * kOpBytes + 256;
+constexpr uint32_t kStageBytes = 2 * (kTileA + kTileB);            // h hi, h lo, W hi, W lo
+constexpr int kPartLd = kBN + 4; // row stride of a segment's sums: 16-byte rows, no bank conflict
+static_assert(kBM * kPartLd * 4 <= kStages * kStageBytes, "partial sums");
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
 constexpr long kWaitLimit = 1L << 24;
 
 // Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B tf32
@@ -119,47 +126,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ float4 tf32_hi(float4 x) {
-  return make_float4(__uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u));
-}
-
-__device__ __forceinline__ void split_tile(const float4 *raw, float4 *hi, float4 *lo, int n4, int tid) {
-  for (int i = tid; i < n4; i += kThreads) {
-    const float4 x = raw[i], h = tf32_hi(x);
-    hi[i] = h;
-    lo[i] = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
-  }
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
-    k_readout_tc(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_w,
+    k_readout_tc(const __grid_constant__ CUtensorMap tm_hh, const __grid_constant__ CUtensorMap tm_hl,
+                 const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl,
                  ReadoutArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles start on 1024-byte boundaries of the shared window.
-  uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t *raw = base;                              // kRaw x [A 16 KB][B 4 KB]
-  uint8_t *ops = raw + kRaw * kRawBytes;            // kOps x [A hi][A lo][B hi][B lo]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(ops + kOps * kOpBytes); // raw_full[kRaw], mma_done[kOps]
-  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(bars + kRaw + kOps);
+  uint8_t *stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u); // [kStages][hh hl wh wl]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(stages + kStages * kStageBytes);   // full[kStages] empty[kStages] done
+  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(bars + 2 * kStages + 1);
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  volatile int *commits_s = abort_s + 1;            // MMA commits issued (thread 0)
-  volatile int *issued_s = abort_s + 2;             // TMA chunks issued (thread 0)
+  // After the MMAs: this segment's sums [row][kPartLd], over the stages.
+  float *part = reinterpret_cast<float *>(stages);
 
+  cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int v0 = blockIdx.x * kBN, b0 = blockIdx.y * kBM;
+  const int v0 = blockIdx.x * kBN, b0 = blockIdx.y * kBM, z = blockIdx.z; // z: k segment = rank in the cluster
   const int nch = (a.K + kKC - 1) / kKC;
   const int segs = nch < kSegs ? nch : kSegs;
-  const uint32_t raw_full0 = smem_u32(bars), mma_done0 = smem_u32(bars + kRaw);
+  // Segment z holds the chunks c with c * segs / nch == z.
+  const int cb = z < segs ? (z * nch + segs - 1) / segs : nch, ce = z < segs ? ((z + 1) * nch + segs - 1) / segs : nch;
+  const int n = ce - cb;
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kStages, done = full0 + 16 * kStages;
 
   if (tid == 0) {
-    for (int i = 0; i < kRaw + kOps; ++i) mbar_init(smem_u32(bars + i), 1);
+    for (int i = 0; i < 2 * kStages + 1; ++i) mbar_init(smem_u32(bars + i), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_s = 0;
-    *commits_s = 0;
-    *issued_s = 0;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -173,102 +166,112 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  auto issue_chunk = [&](int c) {
-    const int rs = c % kRaw;
-    const uint32_t bar = raw_full0 + 8 * rs, dst = smem_u32(raw + rs * kRawBytes);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kRawBytes) : "memory");
-    tma_load_2d(dst, &tm_h, c * kKC, b0, bar);
-    tma_load_2d(dst + kTileA, &tm_w, c * kKC, v0, bar);
-  };
-  if (tid == 0) {
-    const int first = nch < kRaw ? nch : kRaw;
-    for (int c = 0; c < first; ++c) issue_chunk(c);
-    *issued_s = first;
-  }
-
-  bool aborted = false;
-  int seg_prev = -1;
-  for (int c = 0; c < nch; ++c) {
-    const int rs = c % kRaw, os = c % kOps;
-    uint8_t *op = ops + os * kOpBytes;
-    if (!aborted) {
-      bool ok = mbar_wait(raw_full0 + 8 * rs, (c / kRaw) & 1);
-      if (ok && c >= kOps) ok = mbar_wait(mma_done0 + 8 * os, ((c - kOps) / kOps) & 1);
-      if (ok) {
-        const uint8_t *src = raw + rs * kRawBytes;
-        split_tile(reinterpret_cast<const float4 *>(src), reinterpret_cast<float4 *>(op),
-                   reinterpret_cast<float4 *>(op + kTileA), kTileA / 16, tid);
-        split_tile(reinterpret_cast<const float4 *>(src + kTileA), reinterpret_cast<float4 *>(op + 2 * kTileA),
-                   reinterpret_cast<float4 *>(op + 2 * kTileA + kTileB), kTileB / 16, tid);
-      } else {
-        *abort_s = 1;
+  if (tid == 0 && n > 0) {
+    // Local chunk i (global chunk cb + i) lives in stage i % kStages.
+    auto issue_chunk = [&](int i) {
+      const int st = i % kStages;
+      const uint32_t bar = full0 + 8 * st, dst = smem_u32(stages + st * kStageBytes), k = (cb + i) * kKC;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kStageBytes) : "memory");
+      tma_load_2d(dst, &tm_hh, k, b0, bar);
+      tma_load_2d(dst + kTileA, &tm_hl, k, b0, bar);
+      tma_load_2d(dst + 2 * kTileA, &tm_wh, k, v0, bar);
+      tma_load_2d(dst + 2 * kTileA + kTileB, &tm_wl, k, v0, bar);
+    };
+    const int first = n < kStages ? n : kStages;
+    for (int i = 0; i < first; ++i) issue_chunk(i);
+    int issued = first, consumed = 0, committed = 0;
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+      const int st = i % kStages;
+      ok = mbar_wait(full0 + 8 * st, (i / kStages) & 1);
+      if (!ok) break;
+      consumed = i + 1;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t hh = smem_u32(stages + st * kStageBytes), hl = hh + kTileA, wh = hh + 2 * kTileA,
+                     wl = wh + kTileB;
+#pragma unroll
+      for (int j = 0; j < kKC / 8; ++j) {
+        const uint32_t acc = (i == 0 && j == 0) ? 0u : 1u, off = j * 32; // 8 tf32 = 32 bytes along k
+        mma_tf32(tmem, sw128_desc(hh + off), sw128_desc(wh + off), acc);
+        mma_tf32(tmem + kBN, sw128_desc(hl + off), sw128_desc(wh + off), acc);
+        mma_tf32(tmem + kBN, sw128_desc(hh + off), sw128_desc(wl + off), 1u);
+      }
+      mma_commit(empty0 + 8 * st);
+      committed = i + 1;
+      // Refill the previous chunk's stage once its MMAs have read it.
+      const int p = i - 1;
+      if (p >= 0 && p + kStages < n) {
+        ok = mbar_wait(empty0 + 8 * (p % kStages), (p / kStages) & 1);
+        if (ok) issue_chunk(p + kStages), ++issued;
       }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    aborted = *abort_s != 0;
-    const int seg = c * segs / nch;
-    const bool first = seg != seg_prev;
-    seg_prev = seg;
-    if (aborted || tid != 0) continue;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t a_hi = smem_u32(op), a_lo = a_hi + kTileA, w_hi = a_hi + 2 * kTileA, w_lo = w_hi + kTileB;
-    const uint32_t d_main = tmem + seg * kBN, d_corr = tmem + (kSegs + seg) * kBN;
-#pragma unroll
-    for (int j = 0; j < kKC / 8; ++j) {
-      const uint32_t acc = (first && j == 0) ? 0u : 1u, off = j * 32; // 8 tf32 = 32 bytes along k
-      mma_tf32(d_main, sw128_desc(a_hi + off), sw128_desc(w_hi + off), acc);
-      mma_tf32(d_corr, sw128_desc(a_lo + off), sw128_desc(w_hi + off), acc);
-      mma_tf32(d_corr, sw128_desc(a_hi + off), sw128_desc(w_lo + off), 1u);
-    }
-    mma_commit(mma_done0 + 8 * os);
-    *commits_s = c + 1;
-    if (c + kRaw < nch) {
-      issue_chunk(c + kRaw);
-      *issued_s = c + kRaw + 1;
+    if (ok) {
+      mma_commit(done); // arrives once every MMA above has completed
+    } else {
+      *abort_s = 1;
+      // Bounded waits for the work in flight: the last committed MMAs, then
+      // the TMA chunks issued but not consumed.
+      if (committed > 0) mbar_wait(empty0 + 8 * ((committed - 1) % kStages), ((committed - 1) / kStages) & 1);
+      for (int i = consumed; i < issued; ++i) mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1);
     }
   }
   __syncthreads();
-  aborted = *abort_s != 0;
-  const int commits = *commits_s, issued = *issued_s;
-  bool ready = false;
-  if (commits > 0) {
-    const int last = commits - 1;
-    ready = mbar_wait(mma_done0 + 8 * (last % kOps), (last / kOps) & 1);
-  }
-  if (aborted && tid == 0) {
-    // Bounded wait for TMA chunks still landing in this CTA's shared memory.
-    for (int c = commits; c < issued; ++c) mbar_wait(raw_full0 + 8 * (c % kRaw), (c / kRaw) & 1);
-  }
+  const bool aborted = *abort_s != 0;
+  bool ready = n == 0 || (!aborted && mbar_wait(done, 0));
   ready = __syncthreads_and(ready) != 0; // the TMEM loads below are warp-collective
-  if (aborted || !ready) {
-    if (a.err) *reinterpret_cast<volatile int *>(a.err) = 1;
-  } else {
+  const bool good = !aborted && ready;
+  if (!good && a.err) *reinterpret_cast<volatile int *>(a.err) = 1;
+  const int row = warp * 32 + lane;
+  float mainv[32] = {}, corrv[32] = {};
+  if (good && n > 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int b = b0 + warp * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
-    float out[32], part[32];
+    tmem_ld32(lane_base, mainv);
+    tmem_ld32(lane_base + kBN, corrv);
+  }
+  // The segment's sum (main + correction) of each row, into this CTA's shared memory.
+  if (good && n > 0) {
+    float4 *dst = reinterpret_cast<float4 *>(part + row * kPartLd);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) out[j] = (a.bias && v0 + j < a.V) ? a.bias[v0 + j] : 0.f;
-    for (int s = 0; s < 2 * segs; ++s) {
-      const int col = s < segs ? s * kBN : (kSegs + s - segs) * kBN;
-      tmem_ld32(lane_base + col, part);
+    for (int j = 0; j < kBN; j += 4)
+      dst[j / 4] = make_float4(__fadd_rn(mainv[j], corrv[j]), __fadd_rn(mainv[j + 1], corrv[j + 1]),
+                               __fadd_rn(mainv[j + 2], corrv[j + 2]), __fadd_rn(mainv[j + 3], corrv[j + 3]));
+  }
+  cluster.sync(); // every segment's sums are visible cluster-wide
+  if (good) {
+    // This CTA's slice of the rows: bias, then segments 0..segs-1, a fixed
+    // order, read 16 bytes at a time from each segment's shared memory.
+    constexpr int kRowsPer = (kBM + kSegs - 1) / kSegs;
+    const int r0 = z * kRowsPer, r1 = min(kBM, r0 + kRowsPer);
+    for (int it = tid; it < (r1 - r0) * (kBN / 4); it += kThreads) {
+      const int r = r0 + it / (kBN / 4), q = it % (kBN / 4), b = b0 + r, v = v0 + 4 * q;
+      if (b >= a.B) continue;
+      float o[4];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) out[j] = __fadd_rn(out[j], part[j]);
-    }
-    if (b < a.B) {
-      float *y = a.y + (long)b * a.ldy + v0;
-      if (v0 + 32 <= a.V && (a.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0) {
+      for (int e = 0; e < 4; ++e) o[e] = (a.bias && v + e < a.V) ? a.bias[v + e] : 0.f;
+      float4 seg[kSegs];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4 *>(y + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+      for (int sg = 0; sg < kSegs; ++sg)
+        if (sg < segs) seg[sg] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, sg) + r * kPartLd)[q];
+#pragma unroll
+      for (int sg = 0; sg < kSegs; ++sg)
+        if (sg < segs) {
+          o[0] = __fadd_rn(o[0], seg[sg].x);
+          o[1] = __fadd_rn(o[1], seg[sg].y);
+          o[2] = __fadd_rn(o[2], seg[sg].z);
+          o[3] = __fadd_rn(o[3], seg[sg].w);
+        }
+      float *y = a.y + (long)b * a.ldy + v;
+      if (v + 4 <= a.V && (a.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0) {
+        *reinterpret_cast<float4 *>(y) = make_float4(o[0], o[1], o[2], o[3]);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (v0 + j < a.V) y[j] = out[j];
+        for (int e = 0; e < 4; ++e)
+          if (v + e < a.V) y[e] = o[e];
       }
     }
   }
+  cluster.sync(); // every CTA has read the others' sums before any CTA exits
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
@@ -315,8 +318,9 @@ bool readout_tc_enabled() {
 }
 
 bool readout_tc_ok(const ReadoutArgs &a) {
-  return readout_tc_enabled() && a.B >= 2 && a.K >= 4 && a.K % 4 == 0 && a.ldh % 4 == 0 && a.V >= 1 &&
-         aligned16(a.h) && aligned16(a.w) && encode_tiled() != nullptr;
+  return readout_tc_enabled() && a.B >= 2 && a.K >= 4 && a.K % 4 == 0 && a.ldh % 4 == 0 && a.V >= 1 && a.h_hi &&
+         a.h_lo && a.w_hi && a.w_lo && aligned16(a.h_hi) && aligned16(a.h_lo) && aligned16(a.w_hi) &&
+         aligned16(a.w_lo) && encode_tiled() != nullptr;
 }
 
 void configure_readout_tc() {
@@ -327,11 +331,23 @@ const void *readout_tc_kernel() { return reinterpret_cast<const void *>(k_readou
 
 bool launch_readout_tc(const ReadoutArgs &a, cudaStream_t s) {
   if (!readout_tc_ok(a)) return false;
-  CUtensorMap tm_h, tm_w;
-  if (!make_map(&tm_h, a.h, a.B, a.K, a.ldh, kBM) || !make_map(&tm_w, a.w, a.V, a.K, a.K, kBN)) return false;
-  const dim3 grid((a.V + kBN - 1) / kBN, (a.B + kBM - 1) / kBM);
-  k_readout_tc<<<grid, kThreads, kSmemBytes, s>>>(tm_h, tm_w, a);
-  return true;
+  CUtensorMap tm_hh, tm_hl, tm_wh, tm_wl;
+  if (!make_map(&tm_hh, a.h_hi, a.B, a.K, a.ldh, kBM) || !make_map(&tm_hl, a.h_lo, a.B, a.K, a.ldh, kBM) ||
+      !make_map(&tm_wh, a.w_hi, a.V, a.K, a.K, kBN) || !make_map(&tm_wl, a.w_lo, a.V, a.K, a.K, kBN))
+    return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.V + kBN - 1) / kBN, (a.B + kBM - 1) / kBM, kSegs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = kSegs;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_readout_tc, tm_hh, tm_hl, tm_wh, tm_wl, a) == cudaSuccess;
 }
 
 } // namespace ngb
