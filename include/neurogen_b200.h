@@ -166,7 +166,8 @@ typedef struct {
                                    2 = split membrane / push launches,
                                    3 = resident: one persistent launch runs many
                                    ticks with neuron state and delay ring in
-                                   shared memory (CSR storage, unpartitioned).
+                                   shared memory (unpartitioned; its per-owner
+                                   event blocks are built from either storage).
                                    Auto picks 3 when the network fits, else 1
                                    below 65,536 neurons, else 2.                */
   int32_t part_rank, part_world; /* neuron row-partition: this rank owns neurons

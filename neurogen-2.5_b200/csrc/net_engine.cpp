@@ -119,8 +119,8 @@ void validate_config(const ng_net_config &c) {
   if (c.storage != 0 && c.storage != 1) throw std::invalid_argument("storage must be 0 (CSR) or 1 (BSR)");
   if (c.launch < 0 || c.launch > 3)
     throw std::invalid_argument("launch must be 0 (auto), 1 (fused), 2 (split) or 3 (resident)");
-  if (c.launch == 3 && (c.storage != 0 || c.part_world > 1))
-    throw std::invalid_argument("The resident launch needs CSR storage and an unpartitioned network");
+  if (c.launch == 3 && c.part_world > 1)
+    throw std::invalid_argument("The resident launch needs an unpartitioned network");
   switch (c.topology) {
   case NG_TOPO_ERDOS_RENYI:
     if (!(c.p_connect >= 0 && c.p_connect <= 1)) throw std::invalid_argument("p_connect must be in [0, 1]");
@@ -603,9 +603,8 @@ Network::Network(const Topology &topo, const void *nccl_id) : cfg(topo.cfg) {
     for (int x : csr->outdeg) nnz_ += x;
   }
   int max_delay = 1;
-  if (csr)
-    for (uint32_t w : csr->syn) max_delay = std::max(max_delay, int(w >> 28) + 1);
-  init_state(nccl_id, csr != nullptr, max_delay);
+  for (uint32_t w : csr ? csr->syn : bsr->blk) max_delay = std::max(max_delay, int(w >> 28) + 1);
+  init_state(nccl_id, max_delay);
 }
 
 // Partitioned fixed fan-in network whose synapses are drawn on the device:
@@ -628,7 +627,7 @@ Network::Network(const ng_net_config &c, const void *nccl_id, DeviceFanin) : cfg
   d.n_pre = n_pre_;
   d.base = base_;
   generate_fanin_device(lo, hi);
-  init_state(nccl_id, true, c.delay_max);
+  init_state(nccl_id, c.delay_max);
 }
 
 void Network::generate_fanin_device(int lo, int hi) {
@@ -692,7 +691,7 @@ void Network::generate_fanin_device(int lo, int hi) {
 
 // State, counters, launch shape and (partitioned) communicator; the synapses
 // are on the device already.
-void Network::init_state(const void *nccl_id, bool csr, int max_delay) {
+void Network::init_state(const void *nccl_id, int max_delay) {
   const ng_net_config &c = cfg;
   NetDev &d = dev_;
   d.outdeg = outdeg_.as<int>();
@@ -740,7 +739,7 @@ void Network::init_state(const void *nccl_id, bool csr, int max_delay) {
   // the presynaptic groups); tick.
   // Resident launch (persistent kernel, state in shared memory) when asked
   // for, or by default when the network qualifies and fits.
-  if (csr && world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(max_delay, c.launch == 3);
+  if (world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(max_delay, c.launch == 3);
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
   const size_t groups = std::max({pre_groups, (N + kNetBlock - 1) / kNetBlock, size_t(resident_ ? res_.ctas : 0)});
   const size_t bm_words = pre_groups * (kNetBlock / 32);
@@ -793,7 +792,7 @@ bool Network::plan_resident(int max_delay, bool required) {
   if (!coop) return fail("the device has no cooperative launch");
   int dr = 1;
   while (dr < max_delay) dr <<= 1;
-  const bool ev64 = dev_.w_half == 0;
+  const bool ev64 = !dev_.bsr && dev_.w_half == 0; // fp16 weights (block storage is always fp16): 32-bit events
   int P = ((n_ + sms - 1) / sms + 31) / 32 * 32;
   P = std::max(P, std::min(256, (n_ + 31) / 32 * 32));
   if (const char *env = std::getenv("NEUROGEN_RESIDENT_PER_CTA")) P = std::max(P, (std::atoi(env) + 31) / 32 * 32);
@@ -818,8 +817,8 @@ bool Network::plan_resident(int max_delay, bool required) {
   return true;
 }
 
-// Owner blocks from the device CSR: count the overflow blocks, allocate
-// exactly, fill.
+// Owner blocks from the device CSR or block storage: count the overflow
+// blocks, allocate exactly, fill.
 void Network::build_owner_blocks() {
   ResidentDev &r = res_;
   const size_t C = size_t(r.ctas);

@@ -120,7 +120,7 @@ private:
   static constexpr int kResidentChunk = 2048; // ticks per persistent launch
   bool plan_resident(int max_delay, bool required);
   void generate_fanin_device(int lo, int hi);
-  void init_state(const void *nccl_id, bool csr, int max_delay);
+  void init_state(const void *nccl_id, int max_delay);
   void build_owner_blocks();
   void check_resident();
 };

@@ -483,16 +483,45 @@ template <bool HALF> __device__ __forceinline__ bool is_zero(uint32_t bits) {
 
 constexpr int BT = 256;
 
+// Synapses of presynaptic neuron `pre`, by index e.  CSR: entries
+// [row[pre], row[pre+1]).  Block storage: e = block * 16 + r over the blocks of
+// the pre's block-column, i.e. entry r of the pre's column in each 16x16 tile
+// (zero entries are skipped by the callers, as they are by the block push).
+template <bool BSR> __device__ __forceinline__ void edge_range(const NetDev &d, int pre, long long &e0, long long &e1) {
+  if (BSR) {
+    e0 = d.bcol[pre >> 4] * 16;
+    e1 = d.bcol[(pre >> 4) + 1] * 16;
+  } else {
+    e0 = d.row[pre];
+    e1 = d.row[pre + 1];
+  }
+}
+// The synapse word post | (delay - 1) << 28 of entry e.
+template <bool BSR> __device__ __forceinline__ uint32_t edge_word(const NetDev &d, long long e) {
+  if (BSR) {
+    const uint32_t m = d.blk[e >> 4];
+    return ((m & kPostMask) * 16u + (uint32_t)(e & 15)) | (m & ~kPostMask);
+  }
+  return d.syn[e];
+}
+template <bool BSR, bool HALF> __device__ __forceinline__ uint32_t edge_weight(const NetDev &d, int pre, long long e) {
+  if (BSR) return d.tiles[((size_t)(e >> 4) * 16 + (pre & 15)) * 16 + (e & 15)];
+  return weight_bits<HALF>(d, e);
+}
+
 // CTA per presynaptic row: non-zero synapses per owner CTA -> overflow blocks needed.
-template <bool HALF> __global__ void __launch_bounds__(BT) k_owner_count(NetDev d, ResidentDev r,
-                                                                        unsigned long long *need) {
+template <bool BSR, bool HALF> __global__ void __launch_bounds__(BT) k_owner_count(NetDev d, ResidentDev r,
+                                                                                  unsigned long long *need) {
   extern __shared__ int cnt[];
   __shared__ unsigned long long red_s[BT / 32];
   const int pre = blockIdx.x, C = r.ctas, P = r.per_cta;
   for (int q = threadIdx.x; q < C; q += BT) cnt[q] = 0;
   __syncthreads();
-  for (long long e = d.row[pre] + threadIdx.x; e < d.row[pre + 1]; e += BT)
-    if (!is_zero<HALF>(weight_bits<HALF>(d, e))) atomicAdd(&cnt[(int)(d.syn[e] & kPostMask) / P], 1);
+  long long e0, e1;
+  edge_range<BSR>(d, pre, e0, e1);
+  for (long long e = e0 + threadIdx.x; e < e1; e += BT)
+    if (!is_zero<HALF>(edge_weight<BSR, HALF>(d, pre, e)))
+      atomicAdd(&cnt[(int)(edge_word<BSR>(d, e) & kPostMask) / P], 1);
   __syncthreads();
   unsigned long long extra = 0;
   for (int q = threadIdx.x; q < C; q += BT) extra += (unsigned long long)chain_blocks(cnt[q]);
@@ -509,7 +538,7 @@ template <bool HALF> __global__ void __launch_bounds__(BT) k_owner_count(NetDev 
 
 // CTA per presynaptic row: writes its owner blocks (pre-filled with empty
 // words) and allocates overflow blocks from `cursor`.
-template <class E, bool HALF>
+template <class E, bool BSR, bool HALF>
 __global__ void __launch_bounds__(BT) k_owner_fill(NetDev d, ResidentDev r, typename E::word *blocks,
                                                    unsigned long long *cursor, unsigned long long capacity,
                                                    int *err) {
@@ -521,9 +550,11 @@ __global__ void __launch_bounds__(BT) k_owner_fill(NetDev d, ResidentDev r, type
   const unsigned long long primary = (unsigned long long)d.n_pre * C;
   for (int q = threadIdx.x; q < C; q += BT) cnt[q] = cur[q] = 0;
   __syncthreads();
-  const long long e0 = d.row[pre], e1 = d.row[pre + 1];
+  long long e0, e1;
+  edge_range<BSR>(d, pre, e0, e1);
   for (long long e = e0 + threadIdx.x; e < e1; e += BT)
-    if (!is_zero<HALF>(weight_bits<HALF>(d, e))) atomicAdd(&cnt[(int)(d.syn[e] & kPostMask) / P], 1);
+    if (!is_zero<HALF>(edge_weight<BSR, HALF>(d, pre, e)))
+      atomicAdd(&cnt[(int)(edge_word<BSR>(d, e) & kPostMask) / P], 1);
   __syncthreads();
   for (int q = threadIdx.x; q < C; q += BT) {
     const int m = chain_blocks(cnt[q]);
@@ -537,9 +568,9 @@ __global__ void __launch_bounds__(BT) k_owner_fill(NetDev d, ResidentDev r, type
   }
   __syncthreads();
   for (long long e = e0 + threadIdx.x; e < e1; e += BT) {
-    const uint32_t wb = weight_bits<HALF>(d, e);
+    const uint32_t wb = edge_weight<BSR, HALF>(d, pre, e);
     if (is_zero<HALF>(wb)) continue;
-    const uint32_t word = d.syn[e];
+    const uint32_t word = edge_word<BSR>(d, e);
     const int post = (int)(word & kPostMask), q = post / P;
     const int s = atomicAdd(&cur[q], 1), n = cnt[q];
     long long blk = (long long)pre * C + q;
@@ -606,21 +637,27 @@ cudaError_t launch_net_resident(const NetDev &d, const ResidentDev &r, long long
 void launch_owner_count(const NetDev &d, const ResidentDev &r, unsigned long long *need, cudaStream_t s) {
   if (d.n_pre == 0) return;
   const size_t smem = size_t(r.ctas) * 4;
-  if (d.w_half) k_owner_count<true><<<d.n_pre, BT, smem, s>>>(d, r, need);
-  else k_owner_count<false><<<d.n_pre, BT, smem, s>>>(d, r, need);
+  if (d.bsr) k_owner_count<true, true><<<d.n_pre, BT, smem, s>>>(d, r, need);
+  else if (d.w_half) k_owner_count<false, true><<<d.n_pre, BT, smem, s>>>(d, r, need);
+  else k_owner_count<false, false><<<d.n_pre, BT, smem, s>>>(d, r, need);
 }
 
 void launch_owner_fill(const NetDev &d, const ResidentDev &r, void *blocks, unsigned long long *cursor,
                        unsigned long long capacity, int *err, cudaStream_t s) {
   if (d.n_pre == 0) return;
   const size_t smem = size_t(r.ctas) * 16;
-  if (r.ev64) {
-    k_owner_fill<Ev64, false><<<d.n_pre, BT, smem, s>>>(d, r, static_cast<unsigned long long *>(blocks), cursor,
-                                                         capacity, err);
+  if (d.bsr) {
+    // Block storage holds fp16 weights: 32-bit events.
+    if (r.ev64) throw std::logic_error("block storage takes 32-bit owner events");
+    k_owner_fill<Ev32, true, true><<<d.n_pre, BT, smem, s>>>(d, r, static_cast<uint32_t *>(blocks), cursor, capacity,
+                                                              err);
+  } else if (r.ev64) {
+    k_owner_fill<Ev64, false, false><<<d.n_pre, BT, smem, s>>>(d, r, static_cast<unsigned long long *>(blocks),
+                                                                cursor, capacity, err);
   } else {
     if (!d.w_half) throw std::logic_error("32-bit owner events need fp16 weights");
-    k_owner_fill<Ev32, true><<<d.n_pre, BT, smem, s>>>(d, r, static_cast<uint32_t *>(blocks), cursor, capacity,
-                                                        err);
+    k_owner_fill<Ev32, false, true><<<d.n_pre, BT, smem, s>>>(d, r, static_cast<uint32_t *>(blocks), cursor,
+                                                               capacity, err);
   }
 }
 

@@ -51,7 +51,7 @@ def test_isolated_8k_bit_exact_200_ticks(launch):
 
 
 @pytest.mark.parametrize('storage,launch', [('csr', 'fused'), ('csr', 'split'), ('csr', 'resident'),
-                                            ('bsr', 'fused'), ('bsr', 'split')])
+                                            ('bsr', 'fused'), ('bsr', 'split'), ('bsr', 'resident')])
 def test_block_matrix_both_storages_bit_exact(storage, launch):
     cfg = default_config(n=4096, n_exc=3277, topology='bsr16', bsr_blocks=32, bsr_fill=64,
                          weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, storage=storage,
@@ -197,13 +197,15 @@ def test_pipelined_graph_full_size():
     assert b.stats() == (int(ca[:, 0].sum()), int(ca[:, 1].sum()))
 
 
-def test_resident_full_size_equals_split():
-    """N=262,144 fixed fan-in at 5%: the resident launch (state and ring in shared memory, owner
-    blocks with overflow chains) gives every spike, count and state bit of the split launch, across
-    launch boundaries (2,048 ticks a launch) and a resume from an odd tick."""
-    cfg = scaled_262k('csr', rate=0.05)
+@pytest.mark.parametrize('storage', ['csr', 'bsr'])
+def test_resident_full_size_equals_split(storage):
+    """N=262,144 at 5%, fixed fan-in CSR or 16x16 blocks: the resident launch (state and ring in
+    shared memory, owner blocks with overflow chains, built from either storage) gives every spike,
+    count and state bit of the split launch, across launch boundaries (2,048 ticks a launch) and a
+    resume from an odd tick."""
+    cfg = scaled_262k(storage, rate=0.05)
     topo = Topology(cfg)
-    cfg_split = scaled_262k('csr', rate=0.05)
+    cfg_split = scaled_262k(storage, rate=0.05)
     cfg_split.launch = LAUNCH['split']
     res, ref = topo.network(), Topology(cfg_split).network()
     assert res.launch == 'resident' and ref.launch == 'split'
@@ -222,7 +224,7 @@ def test_resident_full_size_equals_split():
 
 def test_auto_launch_choice():
     assert Topology(isolated_8k()).network().launch == 'resident'
-    assert Topology(scaled_262k('bsr', rate=0.03)).network().launch == 'split'
+    assert Topology(scaled_262k('bsr', rate=0.03)).network().launch == 'resident'
     small = default_config(n=1000, launch='split')
     assert Topology(small).network().launch == 'split'
 
