@@ -762,101 +762,132 @@ __global__ void __launch_bounds__(64 * TK_SB) k_tick(TickArgs a) {
 // ---------------------------------------------------------------------------
 // All ticks of one region in one launch: a thread-block cluster of CL CTAs
 // covers the region's c columns (CPC = c / CL each, weights in shared memory).
-// Unit state stays in registers across ticks; each tick's traces go to a
-// shared-memory ping-pong buffer, and the excitatory neighbour term reads the
-// adjacent CTA's edge column through distributed shared memory after a
-// cluster barrier.  Same arithmetic as k_tick, tick for tick.
+// A thread owns one unit of one column for SB sessions: its 64 recurrent
+// weights are read 16 bytes at a time once per 4 k for all SB sessions, and
+// each session's traces 16 bytes at a time (a broadcast to the column's 64
+// threads).  Unit state stays in registers across ticks; each tick's traces
+// go to a shared-memory ping-pong buffer, and the excitatory neighbour term
+// reads the adjacent CTA's edge column through distributed shared memory after
+// a cluster barrier.  Same arithmetic as k_tick, tick for tick: each session's
+// recurrent input is still one sequential 64-term chain.
 // ---------------------------------------------------------------------------
+constexpr int TC_LD = 68; // weight row stride: 16-byte rows, 8 lanes' 16-byte loads hit distinct banks
+
 template <int CPC, int SB>
-__global__ void __launch_bounds__(64 * CPC * SB) k_ticks_cluster(TickArgs a, int ticks) {
+__global__ void __launch_bounds__(64 * CPC) k_ticks_cluster(TickArgs a, int ticks) {
   extern __shared__ __align__(16) float tsm[];
-  float *wt = tsm;                              // [CPC][64][TK_LD]
-  float *trb = tsm + CPC * 64 * TK_LD;          // [2][SB][CPC][64]
+  float *wt = tsm;                              // [CPC][64][TC_LD]
+  float *trb = tsm + CPC * 64 * TC_LD;          // [2][SB][CPC][64]
   cg::cluster_group cluster = cg::this_cluster();
   const int g = blockIdx.x;                     // column group = rank in the cluster
-  const int tid = threadIdx.x, id = tid & 63, cl = (tid >> 6) % CPC, s = tid / (64 * CPC);
-  const int col = g * CPC + cl, b = blockIdx.y * SB + s;
-  const bool live = b < a.B;
+  const int tid = threadIdx.x, id = tid & 63, cl = tid >> 6;
+  const int col = g * CPC + cl, b0 = blockIdx.y * SB;
   {
-    // The CTA's CPC x 4096 recurrent weights: every thread's loads issued
-    // before any store, so the staging costs one L2 round trip.
-    constexpr int NT = 64 * CPC * SB, PER = CPC * 4096 / NT;
-    static_assert(CPC * 4096 % NT == 0, "weight staging");
-    float v[PER];
+    // The CTA's CPC x 4096 recurrent weights, 16-byte cp.async pieces.
+    constexpr int NT = 64 * CPC, PIECES = CPC * 1024 / NT;
+    const float *src = a.rec + (size_t)g * CPC * 4096;
 #pragma unroll
-    for (int u = 0; u < PER; ++u) v[u] = __ldg(a.rec + (size_t)g * CPC * 4096 + tid + u * NT);
-#pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      const int i = tid + u * NT, c = i >> 12, r = i & 4095;
-      wt[c * 64 * TK_LD + (r >> 6) * TK_LD + (r & 63)] = v[u];
+    for (int u = 0; u < PIECES; ++u) {
+      const int p = tid + u * NT, c = p >> 10, r = (p >> 4) & 63, q = p & 15;
+      cp_async16(wt + (c * 64 + r) * TC_LD + q * 4, src + (size_t)p * 4);
     }
+    cp_async_commit();
   }
   const bool exc = (a.tab.exc_mask >> id) & 1ull;
   const int n = a.n, i = col * 64 + id;
-  float *st = a.state + (long)(live ? b : 0) * a.S + a.roff;
-  float V = 0.f, adapt = 0.f, last = 0.f, cnt = 0.f, trace = 0.f, current = 0.f;
-  if (live) {
-    V = st[i];
-    trace = st[n + i];
-    adapt = st[2 * n + i];
-    last = st[3 * n + i];
-    cnt = st[4 * n + a.w + i];
-    current = exc ? .15f : .35f;
-    const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
-    if (a.vin && ii >= 0) current = 3 * host_sigmoid(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii]);
-    if (fi >= 0) current = current + .5f * host_tanh(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi]);
+  float V[SB], trace[SB], adapt[SB], last[SB], cnt[SB], current[SB];
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    const int b = b0 + s;
+    V[s] = trace[s] = adapt[s] = last[s] = cnt[s] = current[s] = 0.f;
+    if (b < a.B) {
+      const float *st = a.state + (long)b * a.S + a.roff;
+      V[s] = st[i];
+      trace[s] = st[n + i];
+      adapt[s] = st[2 * n + i];
+      last[s] = st[3 * n + i];
+      cnt[s] = st[4 * n + a.w + i];
+      float cur = exc ? .15f : .35f;
+      const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
+      if (a.vin && ii >= 0) cur = 3 * host_sigmoid(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii]);
+      if (fi >= 0) cur = cur + .5f * host_tanh(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi]);
+      current[s] = cur;
+    }
   }
   auto tr_at = [&](int buf, int ss, int cc) { return trb + ((buf * SB + ss) * CPC + cc) * 64; };
-  tr_at(0, s, cl)[id] = trace;
-  cluster.sync();
+#pragma unroll
+  for (int s = 0; s < SB; ++s) tr_at(0, s, cl)[id] = trace[s];
+  cp_async_wait<0>();
+  cluster.sync(); // weights and first traces visible
   const float decay = exc ? .6f : .4f;
-  const float *wr = wt + cl * 64 * TK_LD + id * TK_LD;
+  const float *wr = wt + (cl * 64 + id) * TC_LD;
   for (int t = 0; t < ticks; ++t) {
     const int cur = t & 1;
-    const float *mine = tr_at(cur, s, cl);
-    float recurrent = 0.f;
-#pragma unroll 16
-    for (int j = 0; j < 64; ++j) recurrent = __fadd_rn(recurrent, __fmul_rn(wr[j], mine[j]));
-    float neighbor = 0.f;
-    if (exc) {
-      if (col > 0) {
-        const float *left = cl > 0 ? tr_at(cur, s, cl - 1) : cluster.map_shared_rank(tr_at(cur, s, CPC - 1), g - 1);
-        neighbor = neighbor + left[id];
-      }
-      if (col + 1 < a.c) {
-        const float *right = cl + 1 < CPC ? tr_at(cur, s, cl + 1) : cluster.map_shared_rank(tr_at(cur, s, 0), g + 1);
-        neighbor = neighbor + right[id];
+    float recurrent[SB];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) recurrent[s] = 0.f;
+    // Recurrent input, sequential in the presynaptic index (CPUBackend.cpp:28-30).
+#pragma unroll 4
+    for (int q = 0; q < 16; ++q) {
+      const float4 w4 = *reinterpret_cast<const float4 *>(wr + 4 * q);
+#pragma unroll
+      for (int s = 0; s < SB; ++s) {
+        const float4 t4 = *reinterpret_cast<const float4 *>(tr_at(cur, s, cl) + 4 * q);
+        recurrent[s] = __fadd_rn(recurrent[s], __fmul_rn(w4.x, t4.x));
+        recurrent[s] = __fadd_rn(recurrent[s], __fmul_rn(w4.y, t4.y));
+        recurrent[s] = __fadd_rn(recurrent[s], __fmul_rn(w4.z, t4.z));
+        recurrent[s] = __fadd_rn(recurrent[s], __fmul_rn(w4.w, t4.w));
       }
     }
-    const float voltage = decay * V + (1 - decay) * (current + recurrent + .08f * neighbor);
-    const float spike = (voltage - (exc ? 1.f : .6f) - adapt >= 0 ? 1.f : 0.f) * (1 - last);
-    V = voltage * (1 - spike);
-    trace = .8f * trace + .2f * spike;
-    adapt = .98f * adapt + (exc ? .03f : 0.f) * spike;
-    last = spike;
-    cnt = cnt + spike;
-    tr_at(cur ^ 1, s, cl)[id] = trace;
-    const unsigned fired = __ballot_sync(0xffffffffu, live && spike != 0.f);
-    if ((tid & 31) == 0 && fired) atomicAdd(a.spikes + (long)b * a.spikes_ld, __popc(fired));
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+      const bool live = b0 + s < a.B;
+      float neighbor = 0.f;
+      if (exc) {
+        if (col > 0) {
+          const float *left = cl > 0 ? tr_at(cur, s, cl - 1) : cluster.map_shared_rank(tr_at(cur, s, CPC - 1), g - 1);
+          neighbor = neighbor + left[id];
+        }
+        if (col + 1 < a.c) {
+          const float *right = cl + 1 < CPC ? tr_at(cur, s, cl + 1) : cluster.map_shared_rank(tr_at(cur, s, 0), g + 1);
+          neighbor = neighbor + right[id];
+        }
+      }
+      const float voltage = decay * V[s] + (1 - decay) * (current[s] + recurrent[s] + .08f * neighbor);
+      const float spike = (voltage - (exc ? 1.f : .6f) - adapt[s] >= 0 ? 1.f : 0.f) * (1 - last[s]);
+      V[s] = voltage * (1 - spike);
+      trace[s] = .8f * trace[s] + .2f * spike;
+      adapt[s] = .98f * adapt[s] + (exc ? .03f : 0.f) * spike;
+      last[s] = spike;
+      cnt[s] = cnt[s] + spike;
+      tr_at(cur ^ 1, s, cl)[id] = trace[s];
+      const unsigned fired = __ballot_sync(0xffffffffu, live && spike != 0.f);
+      if ((tid & 31) == 0 && fired) atomicAdd(a.spikes + (long)(b0 + s) * a.spikes_ld, __popc(fired));
+    }
     cluster.sync(); // new traces visible cluster-wide; old buffer free for reuse
   }
-  if (!live) return;
-  st[i] = V;
-  st[n + i] = trace;
-  st[2 * n + i] = adapt;
-  st[3 * n + i] = last;
-  st[4 * n + a.w + i] = cnt;
-  const int oi = a.tab.out_idx[id];
-  if (a.feat && oi >= 0) {
-    const int no = a.tab.n_out;
-    float *f = a.feat + (long)b * (2 * a.c * no);
-    f[col * no + oi] = V;
-    f[a.c * no + col * no + oi] = trace;
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    const int b = b0 + s;
+    if (b >= a.B) continue;
+    float *st = a.state + (long)b * a.S + a.roff;
+    st[i] = V[s];
+    st[n + i] = trace[s];
+    st[2 * n + i] = adapt[s];
+    st[3 * n + i] = last[s];
+    st[4 * n + a.w + i] = cnt[s];
+    const int oi = a.tab.out_idx[id];
+    if (a.feat && oi >= 0) {
+      const int no = a.tab.n_out;
+      float *f = a.feat + (long)b * (2 * a.c * no);
+      f[col * no + oi] = V[s];
+      f[a.c * no + col * no + oi] = trace[s];
+    }
   }
 }
 
 template <int CPC, int SB> size_t ticks_cluster_smem() {
-  return sizeof(float) * (CPC * 64 * TK_LD + 2 * SB * CPC * 64);
+  return sizeof(float) * (CPC * 64 * TC_LD + 2 * SB * CPC * 64);
 }
 
 template <int CPC, int SB> void configure_ticks_cluster() {
@@ -867,7 +898,7 @@ template <int CPC, int SB> void configure_ticks_cluster() {
 template <int CPC, int SB> cudaError_t run_ticks_cluster(const TickArgs &a, int ticks, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.c / CPC, (a.B + SB - 1) / SB, 1);
-  cfg.blockDim = dim3(64 * CPC * SB, 1, 1);
+  cfg.blockDim = dim3(64 * CPC, 1, 1);
   cfg.dynamicSmemBytes = ticks_cluster_smem<CPC, SB>();
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -878,6 +909,15 @@ template <int CPC, int SB> cudaError_t run_ticks_cluster(const TickArgs &a, int 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_ticks_cluster<CPC, SB>, a, ticks);
+}
+
+template <int CPC> cudaError_t run_ticks_cluster_sb(const TickArgs &a, int ticks, int sb, cudaStream_t s) {
+  switch (sb) {
+  case 1: return run_ticks_cluster<CPC, 1>(a, ticks, s);
+  case 2: return run_ticks_cluster<CPC, 2>(a, ticks, s);
+  case 4: return run_ticks_cluster<CPC, 4>(a, ticks, s);
+  default: return run_ticks_cluster<CPC, 8>(a, ticks, s);
+  }
 }
 
 __global__ void k_copy_rows(const float *src, long src_ld, float *dst, long dst_ld, int n, int B) {
@@ -959,8 +999,15 @@ void configure_lang_kernels() {
   configure_ticks_cluster<4, 1>();
   configure_ticks_cluster<4, 2>();
   configure_ticks_cluster<4, 4>();
+  configure_ticks_cluster<4, 8>();
+  configure_ticks_cluster<2, 1>();
+  configure_ticks_cluster<2, 2>();
   configure_ticks_cluster<2, 4>();
+  configure_ticks_cluster<2, 8>();
+  configure_ticks_cluster<1, 1>();
+  configure_ticks_cluster<1, 2>();
   configure_ticks_cluster<1, 4>();
+  configure_ticks_cluster<1, 8>();
   configure_gemm<8, 1>();
   configure_gemm<16, 2>();
   configure_gemm<32, 4>();
@@ -1002,8 +1049,15 @@ void preload_lang_kernels() {
                            (const void *)k_ticks_cluster<4, 1>,
                            (const void *)k_ticks_cluster<4, 2>,
                            (const void *)k_ticks_cluster<4, 4>,
+                           (const void *)k_ticks_cluster<4, 8>,
+                           (const void *)k_ticks_cluster<2, 1>,
+                           (const void *)k_ticks_cluster<2, 2>,
                            (const void *)k_ticks_cluster<2, 4>,
+                           (const void *)k_ticks_cluster<2, 8>,
+                           (const void *)k_ticks_cluster<1, 1>,
+                           (const void *)k_ticks_cluster<1, 2>,
                            (const void *)k_ticks_cluster<1, 4>,
+                           (const void *)k_ticks_cluster<1, 8>,
                            (const void *)k_copy_rows,
                            (const void *)k_norm,
                            (const void *)k_activity};
@@ -1116,18 +1170,18 @@ void launch_projection(const ProjArgs &a, cudaStream_t s) {
 
 bool launch_ticks_cluster(const TickArgs &a, int ticks, cudaStream_t s) {
   // Columns per CTA so that the cluster (c / CPC CTAs) is at most 8 wide.
+  const int cpc = (a.c % 4 == 0 && a.c / 4 <= 8) ? 4 : (a.c % 2 == 0 && a.c / 2 <= 8) ? 2 : a.c <= 8 ? 1 : 0;
+  if (!cpc) return false;
+  // Sessions a thread: the most (up to 8) that still give ~1.6 CTAs a SM
+  // (BC-250: 8 at 256 sessions, 1 at 32; measured best at both).
+  // NEUROGEN_TICK_SB = 1 | 2 | 4 | 8 forces one; results do not depend on it.
+  int sb = 8;
+  while (sb > 1 && long(a.c / cpc) * ((a.B + sb - 1) / sb) < 240) sb >>= 1;
+  if (const char *v = std::getenv("NEUROGEN_TICK_SB")) sb = std::atoi(v);
   cudaError_t e;
-  if (a.c % 4 == 0 && a.c / 4 <= 8) {
-    if (a.B == 1) e = run_ticks_cluster<4, 1>(a, ticks, s);
-    else if (a.B == 2) e = run_ticks_cluster<4, 2>(a, ticks, s);
-    else e = run_ticks_cluster<4, 4>(a, ticks, s);
-  } else if (a.c % 2 == 0 && a.c / 2 <= 8) {
-    e = run_ticks_cluster<2, 4>(a, ticks, s);
-  } else if (a.c <= 8) {
-    e = run_ticks_cluster<1, 4>(a, ticks, s);
-  } else {
-    return false;
-  }
+  if (cpc == 4) e = run_ticks_cluster_sb<4>(a, ticks, sb, s);
+  else if (cpc == 2) e = run_ticks_cluster_sb<2>(a, ticks, sb, s);
+  else e = run_ticks_cluster_sb<1>(a, ticks, sb, s);
   if (e != cudaSuccess) throw std::runtime_error(std::string("cluster tick launch: ") + cudaGetErrorString(e));
   return true;
 }

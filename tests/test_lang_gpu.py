@@ -276,6 +276,9 @@ print('ok')
     (6, 3, 5),    # cluster of 3, two columns each, ragged session tile
     (9, 3, 3),    # no cluster shape: one launch per tick
     (1, 1, 1),    # single column, single tick
+    (4, 2, 3),    # one CTA of four columns
+    (8, 2, 70),   # cluster of 2 CTAs, many sessions
+    (2, 3, 9),    # one CTA of two columns
 ])
 def test_tick_paths_match_reference(columns, ticks, batch):
     """Every tick-kernel shape (cluster widths, columns per CTA, the per-tick fallback) against
@@ -385,3 +388,25 @@ def test_tensor_core_readout_ragged_k_and_fallback(monkeypatch):
         lbt, _, _, _ = eng.step_batch(np.full(B, 5), sb)
         assert np.array_equal(l1, l1s) and np.array_equal(lbs[0], l1s[0])
         assert np.array_equal(lbt, lbs) != tc
+
+
+@pytest.mark.parametrize('sb', ['2', '4', '8'])
+def test_tick_sessions_per_thread_bit_identical(sb, monkeypatch):
+    """The recurrent tick kernel with 2, 4 or 8 sessions a thread (ragged last CTA) gives the bits
+    of one session a thread, for 4-, 2- and 1-column CTAs."""
+    for columns in (8, 6, 3):
+        cfg = LanguageConfig(columns=columns, width=24, regions=2, ticks=3, idle_steps=1)
+        w = init_packed_weights(cfg, seed=columns)
+        rng = np.random.default_rng(columns)
+        w = (w + rng.normal(0, 0.2, w.size)).astype(np.float32)
+        eng = NativeEngine(cfg, w)
+        B = 13
+        toks = rng.integers(0, 264, (4, B))
+        out = {}
+        for mode in ('1', sb):
+            monkeypatch.setenv('NEUROGEN_TICK_SB', mode)
+            st = np.zeros((B, eng.state_size), np.float32)
+            for t in range(4):
+                lg, st, _, _ = eng.step_batch(toks[t], st)
+            out[mode] = (lg, st)
+        assert np.array_equal(out['1'][0], out[sb][0]) and np.array_equal(out['1'][1], out[sb][1])
