@@ -229,11 +229,12 @@ class NativeLanguageModel:
     (hidden, state, activity), as the reference does.
     """
 
-    def __init__(self, config, weights, model=None):
+    def __init__(self, config, weights, model=None, state_dict=None):
         self.config = config
         self.engine = NativeEngine(config, weights)
         self.native_backend = self.engine.backend
         self.model = model
+        self._state_dict = state_dict  # checkpoint tensors for the audio projection and head (listen)
         self._versions = self._param_versions()
 
     @classmethod
@@ -248,8 +249,8 @@ class NativeLanguageModel:
     def from_checkpoint(cls, path, backend='native-cuda'):
         if backend not in NATIVE_DEVICES:
             raise ValueError(f'Unknown native device: {backend}')
-        config, weights, _ = load_checkpoint(path)
-        return cls(config, weights)
+        config, weights, payload = load_checkpoint(path)
+        return cls(config, weights, state_dict=payload['model'])
 
     def _param_versions(self):
         if self.model is None:
@@ -343,6 +344,39 @@ class NativeLanguageModel:
         return torch.stack(outputs, 1), state, torch.stack(activity).mean(), torch.stack(hidden, 1)
 
     forward = __call__
+
+    def _audio_and_head(self):
+        if self.model is not None:
+            return self.model.audio_input, self.model.head
+        sd = self._state_dict
+        if sd is None or 'audio_input.weight' not in sd:
+            raise ValueError('listen needs the audio projection: build from a model or a checkpoint')
+        c = self.config
+        audio, head = torch.nn.Linear(c.mel_bins, c.width), torch.nn.Linear(c.width, VOCAB)
+        with torch.no_grad():
+            audio.weight.copy_(sd['audio_input.weight'])
+            audio.bias.copy_(sd['audio_input.bias'])
+            head.weight.copy_(sd['head.weight'])
+            head.bias.copy_(sd['head.bias'])
+        return audio.eval(), head.eval()
+
+    def listen(self, features, state=None):
+        """Mel frames [batch, time, mel_bins]: each frame through the audio projection and one
+        ``advance`` (non-idle), logits from the head (reference LanguageModel.listen,
+        model.py:152-158).  The two projections run in torch, as in the reference; the advance runs
+        on the GPU engine."""
+        if features.ndim != 3 or features.shape[2] != self.config.mel_bins:
+            raise ValueError('Native listen features must have shape [batch, time, mel_bins]')
+        audio, head = self._audio_and_head()
+        logits, activity = [], []
+        with torch.no_grad():
+            for frame in features.unbind(1):
+                h, state, spikes = self.advance(audio(frame.float()), state)
+                logits.append(head(h))
+                activity.append(spikes)
+        if not logits:
+            raise ValueError('Need at least one feature frame')
+        return torch.stack(logits, 1), state, torch.stack(activity).mean()
 
 
 def config_dict(config):

@@ -410,3 +410,33 @@ def test_tick_sessions_per_thread_bit_identical(sb, monkeypatch):
                 lg, st, _, _ = eng.step_batch(toks[t], st)
             out[mode] = (lg, st)
         assert np.array_equal(out['1'][0], out[sb][0]) and np.array_equal(out['1'][1], out[sb][1])
+
+
+def test_listen_matches_reference_advance_and_head():
+    """listen (reference model.py:152-158): each mel frame through the audio projection, one
+    non-idle advance on the GPU engine, logits from the head; against the reference library's
+    advance with the same projections."""
+    import torch
+    from neurogen_b200.language import NativeLanguageModel
+    cfg = LanguageConfig(columns=3, width=24, regions=2, ticks=2, idle_steps=1, mel_bins=8)
+    w = init_packed_weights(cfg, seed=5)
+    torch.manual_seed(1)
+    audio = torch.nn.Linear(cfg.mel_bins, cfg.width)
+    W, bias = head_weights(cfg, w)
+    sd = {'audio_input.weight': audio.weight.detach().clone(), 'audio_input.bias': audio.bias.detach().clone(),
+          'head.weight': torch.from_numpy(W.astype(np.float32)), 'head.bias': torch.from_numpy(bias.astype(np.float32))}
+    model = NativeLanguageModel(cfg, w, state_dict=sd)
+    feats = torch.randn(2, 5, cfg.mel_bins)
+    logits, state, act = model.listen(feats)
+    assert tuple(logits.shape) == (2, 5, 264)
+    ref = RefEngine(cfg, w)
+    with torch.no_grad():
+        for b in range(2):
+            s = np.zeros(ref.S, np.float32)
+            for t in range(5):
+                x = audio(feats[b, t]).numpy()
+                h, s, _ = ref.advance(x, s, False)
+                want = (torch.from_numpy(h) @ sd['head.weight'].T + sd['head.bias']).numpy()
+                np.testing.assert_allclose(logits[b, t].numpy(), want, rtol=1e-4, atol=1e-5)
+    with pytest.raises(ValueError, match='mel_bins'):
+        model.listen(torch.zeros(2, 3, cfg.mel_bins + 1))
