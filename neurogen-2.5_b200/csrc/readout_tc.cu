@@ -347,7 +347,13 @@ bool launch_readout_tc(const ReadoutArgs &a, cudaStream_t s) {
   attr[0].val.clusterDim.z = kSegs;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_readout_tc, tm_hh, tm_hl, tm_wh, tm_wl, a) == cudaSuccess;
+  if (cudaLaunchKernelEx(&cfg, k_readout_tc, tm_hh, tm_hl, tm_wh, tm_wl, a) != cudaSuccess) {
+    // A device that cannot place the cluster: clear the launch error; the
+    // caller runs the SIMT readout instead.
+    (void)cudaGetLastError();
+    return false;
+  }
+  return true;
 }
 
 } // namespace ngb
