@@ -396,14 +396,21 @@ def lang_flops_per_token(cfg):
 
 
 def lang_launches_per_token(cfg):
-    """Kernels one pool token step enqueues (lang_engine.cpp DeviceModel::enqueue)."""
+    """Kernels one pool token step enqueues (lang_engine.cpp DeviceModel::enqueue_view): per advance the
+    regions' feedback projections in batches of four, then per region the input projection (sensory
+    regions), the recurrent ticks (one cluster launch, or one launch per tick plus a copy for odd tick
+    counts when no cluster shape fits the column count), the output projection and the LayerNorm; per
+    token the readout and the activity."""
+    c = cfg.columns
+    cluster = (c % 4 == 0 and c // 4 <= 8) or (c % 2 == 0 and c // 2 <= 8) or c <= 8
+    ticks = 1 if cluster else cfg.ticks + cfg.ticks % 2
     per = 0
     for adv in range(1 + cfg.idle_steps):
-        per += cfg.regions  # feedback projections
+        per += -(-cfg.regions // 4)
         for r in range(cfg.regions):
             sensory = adv == 0 or r > 0
-            per += int(sensory) + cfg.ticks + (cfg.ticks % 2) + 2  # input, ticks, copy, output, norm
-    return per + 2  # head, activity
+            per += int(sensory) + ticks + 2
+    return per + 2
 
 
 def bench_lang(args, dist):

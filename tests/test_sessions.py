@@ -39,3 +39,22 @@ def test_our_payload_has_the_reference_fields(tmp_path):
         for a, b in zip(r1, r2):
             assert torch.equal(a, b)
     assert np.array_equal(back['logits'].numpy(), ref['logits'].numpy())
+
+
+def test_bench_counts_the_engines_launches_per_token():
+    """bench.py's gpu_launches claim for a BC-250 token step equals the kernels the engine enqueues:
+    2 advances x (1 batched feedback + 4 regions x (input, cluster ticks, output, LayerNorm)) less
+    region 0's idle input, plus readout and activity = 35 (the ncu launch list of two pool token steps
+    holds 70 kernels)."""
+    import importlib.util
+    from pathlib import Path
+    from neurogen_b200.language import LanguageConfig
+    spec = importlib.util.spec_from_file_location('bench', Path(__file__).resolve().parents[1] / 'bench.py')
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench.lang_launches_per_token(LanguageConfig()) == 35
+    # No cluster shape for 9 columns: one launch per tick plus a copy for an odd tick count.
+    # Advance 0: feedback + 2 x (input, 3 ticks + copy, output, norm); idle advance: feedback, region 0
+    # without input, region 1 with; readout, activity.
+    assert bench.lang_launches_per_token(LanguageConfig(columns=9, width=24, regions=2, ticks=3, idle_steps=1)) == \
+        (1 + 2 * 7) + (1 + 6 + 7) + 2
