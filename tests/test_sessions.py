@@ -58,3 +58,23 @@ def test_bench_counts_the_engines_launches_per_token():
     # without input, region 1 with; readout, activity.
     assert bench.lang_launches_per_token(LanguageConfig(columns=9, width=24, regions=2, ticks=3, idle_steps=1)) == \
         (1 + 2 * 7) + (1 + 6 + 7) + 2
+
+
+def test_bench_algorithmic_bytes_per_tick():
+    """The roofline numerator for the scaled tick: CSR events x (4 B index + 2 B fp16 weight + 1 B
+    delay) + N x 48 B of state and ring slot + N/8 spike bits; block storage: per spiking neuron and
+    block of its block-column a 32-byte tile column and a 4-byte block word.  At a 3% rate these are
+    the 40.8 MB and 48.9 MB a tick the roofline fractions are quoted on."""
+    import importlib.util
+    from pathlib import Path
+    from neurogen_b200.network import scaled_262k
+    spec = importlib.util.spec_from_file_location('bench', Path(__file__).resolve().parents[1] / 'bench.py')
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    n = 262144
+    spikes = 0.03 * n
+    csr, bsr = scaled_262k('csr'), scaled_262k('bsr')
+    assert bench.tick_bytes(csr, spikes, spikes * 512) == n * 48 + n / 8 + spikes * 512 * 7
+    assert bench.tick_bytes(bsr, spikes, spikes * 512) == n * 48 + n / 8 + spikes * 128 * 36
+    assert abs(bench.tick_bytes(csr, spikes, spikes * 512) / 1e6 - 40.8) < 0.1
+    assert abs(bench.tick_bytes(bsr, spikes, spikes * 512) / 1e6 - 48.9) < 0.1
