@@ -84,7 +84,10 @@ int ng_advance_batch(void *engine, const float *inputs, int batch,
  * of working memory are rejected with an error (BC-250 needs ~57k).  The
  * first call on a device looks the array up and loads the kernels; make it
  * before any stream capture.  Calls share the array: this process serialises
- * them, and calls that overlap on the GPU from other means would race. */
+ * them per device, and calls that overlap on the GPU from other means would
+ * race.  The array's address is looked up once per device and kept: the
+ * library assumes the device's primary context lives as long as the process
+ * (after a cudaDeviceReset, create the engine anew in a new process). */
 int ng_step_static(void *engine, int token, const float *state,
                    size_t state_count, float *next_state, float *logits,
                    float *hidden, float *activity);

@@ -37,7 +37,9 @@ __device__ __align__(256) float g_step_scratch[kStepScratchFloats];
 // this address, never `g_step_scratch` itself.
 constexpr int kMaxDevices = 64;
 float *g_scratch_addr[kMaxDevices] = {};
-std::mutex g_scratch_mutex; // calls share the array: one call at a time per process
+// Each device holds its own copy of the array, so calls are serialised per
+// device: static steps on different GPUs run side by side.
+std::mutex g_scratch_mutex[kMaxDevices];
 
 // First call on a device (that device current): look the array up and load
 // every language-core kernel, so that no later call makes the driver load
@@ -96,8 +98,9 @@ extern "C" int ng_step_static(void *p, int token, const float *state, size_t sta
     if (!next_state || !logits || !hidden || !activity) throw std::invalid_argument("Null output");
     if (token < 0 || token >= kVocab) throw std::invalid_argument("Token must be in 0..263");
     std::lock_guard<std::mutex> lock(e.mutex);
-    std::lock_guard<std::mutex> scratch_lock(g_scratch_mutex);
     DeviceModel &m = e.device();
+    if (m.device < 0 || m.device >= kMaxDevices) throw std::runtime_error("CUDA device index out of range");
+    std::lock_guard<std::mutex> scratch_lock(g_scratch_mutex[m.device]);
     const StepLayout L(m.dims);
     if (L.total > kStepScratchFloats)
       throw std::invalid_argument("ng_step_static: this model needs " + std::to_string(L.total) +
@@ -122,5 +125,6 @@ extern "C" int ng_step_static(void *p, int token, const float *state, size_t sta
     NGB_CUDA(cudaMemcpyAsync(hidden, d_hidden, size_t(w) * sizeof(float), cudaMemcpyDeviceToHost, st));
     NGB_CUDA(cudaMemcpyAsync(activity, d_act, sizeof(float), cudaMemcpyDeviceToHost, st));
     NGB_CUDA(cudaStreamSynchronize(st));
+    m.check_device_errors(); // same error reporting as ng_step
   });
 }

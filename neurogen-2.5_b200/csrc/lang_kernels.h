@@ -58,6 +58,9 @@ struct ReadoutArgs {
   long ldy;
   int B, K, V;
   int *err;
+  // Test switch: non-zero makes the launch give up before it issues any copy
+  // or MMA, as a wait that ran out would (set by launch_readout_tc only).
+  int stall_test;
 };
 // False when NEUROGEN_READOUT=simt is set (the sequential SIMT projection is
 // then used at every batch size).

@@ -31,6 +31,7 @@
 
 #include <cooperative_groups.h>
 #include <cuda.h>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -166,7 +167,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (tid == 0 && n > 0) {
+  if (tid == 0 && n > 0 && a.stall_test) {
+    // Test switch: the abort path of a wait that ran out, with nothing in
+    // flight yet (no copy or MMA has been issued).
+    *abort_s = 1;
+  } else if (tid == 0 && n > 0) {
     // Local chunk i (global chunk cb + i) lives in stage i % kStages.
     auto issue_chunk = [&](int i) {
       const int st = i % kStages;
@@ -329,8 +334,25 @@ void configure_readout_tc() {
 
 const void *readout_tc_kernel() { return reinterpret_cast<const void *>(k_readout_tc); }
 
-bool launch_readout_tc(const ReadoutArgs &a, cudaStream_t s) {
-  if (!readout_tc_ok(a)) return false;
+// Test switch NEUROGEN_TEST_READOUT_STALL=k: the first k tensor-core readout
+// launches of the process take the kernel's timeout path before issuing any
+// copy or MMA, so the error report and the recovery after it can be tested
+// without a wait actually running out.
+static int take_readout_stall() {
+  static std::atomic<int> left{[] {
+    const char *e = std::getenv("NEUROGEN_TEST_READOUT_STALL");
+    return e ? std::atoi(e) : 0;
+  }()};
+  int k = left.load();
+  while (k > 0 && !left.compare_exchange_weak(k, k - 1)) {
+  }
+  return k > 0 ? 1 : 0;
+}
+
+bool launch_readout_tc(const ReadoutArgs &args, cudaStream_t s) {
+  if (!readout_tc_ok(args)) return false;
+  ReadoutArgs a = args;
+  a.stall_test = take_readout_stall();
   CUtensorMap tm_hh, tm_hl, tm_wh, tm_wl;
   if (!make_map(&tm_hh, a.h_hi, a.B, a.K, a.ldh, kBM) || !make_map(&tm_hl, a.h_lo, a.B, a.K, a.ldh, kBM) ||
       !make_map(&tm_wh, a.w_hi, a.V, a.K, a.K, kBN) || !make_map(&tm_wl, a.w_lo, a.V, a.K, a.K, kBN))

@@ -440,3 +440,41 @@ def test_listen_matches_reference_advance_and_head():
                 np.testing.assert_allclose(logits[b, t].numpy(), want, rtol=1e-4, atol=1e-5)
     with pytest.raises(ValueError, match='mel_bins'):
         model.listen(torch.zeros(2, 3, cfg.mel_bins + 1))
+
+
+READOUT_STALL_CHILD = r'''
+import sys
+sys.path[:0] = {paths!r}
+import numpy as np
+from neurogen_b200.language import LanguageConfig, NativeEngine, init_packed_weights
+cfg = LanguageConfig(columns=2, width=32, regions=2, ticks=2, idle_steps=1)
+eng = NativeEngine(cfg, init_packed_weights(cfg, seed=2))
+s = np.zeros((4, eng.state_size), np.float32)
+try:
+    eng.step_batch(np.array([1, 2, 3, 4]), s)
+    print('no error')
+except ValueError as e:
+    print('raised:', e)
+l1, s1, _, _ = eng.step_batch(np.array([1, 2, 3, 4]), s)     # same engine, the next step
+fresh = NativeEngine(cfg, init_packed_weights(cfg, seed=2))
+l2, s2, _, _ = fresh.step_batch(np.array([1, 2, 3, 4]), s)
+print('after:', bool(np.array_equal(l1, l2) and np.array_equal(s1, s2)))
+'''
+
+
+def test_readout_wait_runs_out_cleanly(tmp_path):
+    """The tensor-core readout's waits are bounded.  A test switch makes the first readout launch
+    take the timeout path before it issues any copy or MMA: the batched step reports
+    'Readout kernel timed out', and the next step on the same engine runs normally and equals a
+    fresh engine's."""
+    import os
+    import subprocess
+    import sys
+    script = tmp_path / 'stall.py'
+    script.write_text(READOUT_STALL_CHILD.format(paths=[str(p) for p in sys.path[:3]]))
+    env = dict(os.environ, NEUROGEN_TEST_READOUT_STALL='1')
+    env.pop('NEUROGEN_READOUT', None)
+    out = subprocess.run([sys.executable, str(script)], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-3000:]
+    assert 'raised: Readout kernel timed out' in out.stdout, out.stdout
+    assert 'after: True' in out.stdout, out.stdout

@@ -1,0 +1,169 @@
+"""Parity at the exact benchmark configurations the throughput numbers are quoted on.
+
+Bars (the contract of this backend): spike indices identical for the first 100 ticks, state
+within 1e-5 relative, logits within 1e-4 relative; the isolated-tick network is bit-exact with
+its fp32 oracle by construction.
+
+* Scaled tick, N=262,144, fan-in 512 CSR and the 16x16 block matrix, imposed Bernoulli(0.03)
+  spikes, the resident launch the benchmark times: 100 ticks against oracle/net_oracle.c, every
+  spike and synaptic-event count of every tick and the whole state (V, adaptation, g_E, g_I,
+  refractory counters, every delay-ring slot) after 50 and after 100 ticks.
+* BC-250 seed-0 profile at batch 1, free-running over the 512-token benchmark stream (each side
+  continues from its own state) against the reference's own native library: every step's
+  logits, state and spikes; the first spike divergence, if any, is reported.
+* BC-250 seed-0 profile, 256 independent sessions (session k fed its own seeded stream) through
+  one device-resident pool, 16 tokens: every session against its own reference engine run;
+  the pool's token readout runs on the tensor cores, so its logits are held to 1e-4 relative
+  with a floor of 1e-4 of the row's largest logit.
+"""
+import os
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+
+from neurogen_b200.language import LanguageConfig, NativeEngine, init_packed_weights
+from neurogen_b200.network import Topology, scaled_262k
+from oracle.lang import RefEngine
+from oracle.net import NetOracle
+
+pytestmark = pytest.mark.gpu
+
+STATE_RTOL, STATE_ATOL = 1e-5, 1e-6
+LOGIT_RTOL, LOGIT_ATOL = 1e-4, 1e-6
+STATE_KEYS = ('v', 'a', 'ge', 'gi', 'ref', 'ring')
+
+
+def region_fields(cfg, state):
+    """Per region: (voltage, trace, adaptation, last_spikes, memory, counts) of a packed state."""
+    n, w = cfg.columns * 64, cfg.width
+    rs = 5 * n + w
+    out = []
+    for r in range(cfg.regions):
+        b = state[..., r * rs:(r + 1) * rs]
+        out.append(dict(v=b[..., :n], trace=b[..., n:2 * n], adapt=b[..., 2 * n:3 * n], last=b[..., 3 * n:4 * n],
+                        mem=b[..., 4 * n:4 * n + w], counts=b[..., 4 * n + w:]))
+    return out
+
+
+def spikes_equal(cfg, a, b):
+    return all(np.array_equal(x['last'], y['last']) and np.array_equal(x['counts'], y['counts'])
+               for x, y in zip(region_fields(cfg, a), region_fields(cfg, b)))
+
+
+def assert_state_close(cfg, got, want, where=''):
+    for r, (x, y) in enumerate(zip(region_fields(cfg, got), region_fields(cfg, want))):
+        np.testing.assert_array_equal(x['last'], y['last'], err_msg=f'{where} region {r} spikes')
+        np.testing.assert_array_equal(x['counts'], y['counts'], err_msg=f'{where} region {r} counts')
+        for k in ('v', 'trace', 'adapt', 'mem'):
+            np.testing.assert_allclose(x[k], y[k], rtol=STATE_RTOL, atol=STATE_ATOL, err_msg=f'{where} region {r} {k}')
+
+
+# ---------------------------------------------------------------------------
+# Scaled tick, N=262,144 (resident launch), 100 ticks against the oracle.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize('storage', ['csr', 'bsr'])
+def test_scaled_262k_resident_100_ticks_vs_oracle(storage):
+    cfg = scaled_262k(storage, rate=0.03)
+    topo = Topology(cfg)
+    net = topo.network()
+    assert net.launch == 'resident'
+    orc = NetOracle(cfg, *topo.export())
+    events = 0
+    for half in range(2):
+        gs, gc = net.run(50)
+        os_, oc = orc.run(50)
+        np.testing.assert_array_equal(gs, os_)   # every spike of every tick
+        np.testing.assert_array_equal(gc, oc)    # spikes and delivered synaptic events per tick
+        a, b = net.get_state(), orc.get_state()
+        for k in STATE_KEYS:
+            assert np.array_equal(a[k], b[k]), (half, k)
+        assert a['tick'] == b['tick'] == 50 * (half + 1)
+        events += int(gc[:, 1].sum())
+    print(f'{storage}: 100 ticks bit-exact, {events / 100:,.0f} synaptic events a tick')
+    assert events > 100 * 3.5e6
+
+
+# ---------------------------------------------------------------------------
+# BC-250 batch 1, free-running over the 512-token stream.
+# ---------------------------------------------------------------------------
+def test_bc250_free_running_512_tokens_vs_reference(golden_lang):
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng, ref = NativeEngine(cfg, w), RefEngine(cfg, w)
+    toks = golden_lang['bc250_tokens']
+    sg = np.zeros((1, ref.S), np.float32)
+    sr = sg[0].copy()
+    first_diverging = None
+    identical = 0
+    worst_state = worst_logit = 0.0
+    for i, tok in enumerate(toks):
+        lg, sg, ag, hg = eng.step_batch(np.array([tok]), sg)
+        lr, sr, ar, hr = ref.step(int(tok), sr)
+        if first_diverging is None and not spikes_equal(cfg, sg[0], sr):
+            first_diverging = i
+        np.testing.assert_allclose(lg[0], lr, rtol=LOGIT_RTOL, atol=LOGIT_ATOL, err_msg=f'token {i}')
+        assert_state_close(cfg, sg[0], sr, where=f'token {i}')
+        np.testing.assert_allclose(hg[0], hr, rtol=1e-4, atol=1e-6, err_msg=f'token {i}')
+        d = np.abs(sg[0].astype(np.float64) - sr) / np.maximum(np.abs(sr), 1e-6)
+        worst_state = max(worst_state, float(d.max()))
+        worst_logit = max(worst_logit, float((np.abs(lg[0].astype(np.float64) - lr) /
+                                              np.maximum(np.abs(lr), 1e-6)).max()))
+        identical += int(np.array_equal(sg[0], sr) and np.array_equal(lg[0], lr))
+    # One token is two advances of two ticks per region: 512 tokens = 2,048 ticks per region.
+    print(f'BC-250 free-running 512 tokens: first spike divergence at token {first_diverging}; '
+          f'bit-identical steps {identical}/512; worst relative state {worst_state:.2e}, logits {worst_logit:.2e}')
+    assert first_diverging is None
+
+
+# ---------------------------------------------------------------------------
+# BC-250, 256 sessions through one device pool, 16 tokens.
+# ---------------------------------------------------------------------------
+def session_streams(sessions, tokens):
+    """Session k's stream: torch.randint(0, 264, (1024,)) with generator seed k."""
+    import torch
+    cols = []
+    for k in range(sessions):
+        g = torch.Generator().manual_seed(k)
+        cols.append(torch.randint(0, 264, (1024,), generator=g).numpy()[:tokens])
+    return np.stack(cols, 1).astype(np.int32)   # [tokens, sessions]
+
+
+def test_bc250_256_session_pool_16_tokens_vs_reference():
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    eng = NativeEngine(cfg, w)
+    lib = eng.lib
+    B, T = 256, 16
+    toks = session_streams(B, T)
+    workers = max(1, min(32, os.cpu_count() or 1))
+    engines = [RefEngine(cfg, w) for _ in range(workers)]
+    ref_state = np.zeros((B, engines[0].S), np.float32)
+    ref_logits = np.zeros((B, 264), np.float32)
+
+    def ref_slice(k, t):
+        for b in range(k, B, workers):
+            ref_logits[b], ref_state[b], _, _ = engines[k].step(int(toks[t, b]), ref_state[b])
+
+    pool = lib.ng_pool_create(eng.handle, B)
+    assert pool, lib.ng_error().decode()
+    try:
+        logits = np.zeros((B, 264), np.float32)
+        state = np.zeros((B, eng.state_size), np.float32)
+        worst = 0.0
+        with ThreadPoolExecutor(workers) as ex:
+            for t in range(T):
+                row = np.ascontiguousarray(toks[t])
+                assert lib.ng_pool_step(pool, row, logits.ctypes.data, None, None) == 0, lib.ng_error().decode()
+                list(ex.map(lambda k: ref_slice(k, t), range(workers)))
+                assert lib.ng_pool_store(pool, state) == 0
+                for b in range(B):
+                    assert_state_close(cfg, state[b], ref_state[b], where=f'token {t} session {b}')
+                # 1e-4 relative elementwise, with a floor of 1e-4 of the row's largest logit.
+                scale = np.abs(ref_logits).max(axis=1, keepdims=True)
+                err = np.abs(logits.astype(np.float64) - ref_logits) - LOGIT_RTOL * np.abs(ref_logits)
+                assert (err <= LOGIT_RTOL * scale).all(), f'token {t}: logits beyond 1e-4 (row floor)'
+                worst = max(worst, float((np.abs(logits.astype(np.float64) - ref_logits) / scale).max()))
+        print(f'256 sessions x {T} tokens: spikes exact, state 1e-5; worst |logit error| / row max {worst:.2e}')
+    finally:
+        lib.ng_pool_destroy(pool)

@@ -55,6 +55,24 @@ def test_static_step_matches_ng_step_on_two_calls_in_a_row(cfg, seed):
         s_ref, s_new = ref[0], new[0]
 
 
+def test_warm_static_step_allocates_no_device_memory():
+    """After a first call (which looks the array up and loads the kernels), further calls leave
+    the device's free memory exactly unchanged: nothing is allocated per call."""
+    import torch
+    cfg = LanguageConfig()
+    eng = NativeEngine(cfg, init_packed_weights(cfg, seed=0))
+    lib = eng.lib
+    s = np.zeros(eng.state_size, np.float32)
+    s = step(eng, cfg, lib.ng_step_static, 257, s)[0]
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for token in (104, 101, 108, 108, 111):
+        s = step(eng, cfg, lib.ng_step_static, token, s)[0]
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+
+
 def test_static_step_rejects_models_beyond_its_buffer():
     # 1,024 columns of one region: a 327,696-float state, more than the 262,144-float buffer.
     cfg = LanguageConfig(columns=1024, width=16, regions=1, ticks=1, idle_steps=0)
