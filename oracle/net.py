@@ -37,11 +37,81 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(ct.c_void_p)
 
 
+# Defaults of the engine's network configuration (biology.py's BiologyConfig and membrane
+# constants, biology.py:19-77, 153-170), restated here so that the CPU legs need no CUDA library.
+DEFAULTS = dict(n=1024, n_exc=819, topology=0, p_connect=0.02, fanin=512, bsr_blocks=128, bsr_fill=64,
+                weight_kind=0, w_mu=-2.0, w_sigma=0.5, delay_min=1, delay_max=8, seed=0, dt_ms=1.0,
+                cap_exc_pf=200.0, cap_inh_pf=100.0, g_leak_ns=10.0, e_leak_mv=-65.0, e_inh_mv=-80.0,
+                v_thresh_mv=-50.0, v_reset_mv=-65.0, t_ref_ms=2.0, tau_exc_ms=5.0, tau_inh_ms=10.0,
+                tau_adapt_ms=200.0, adapt_inc_pa=15.0, bias_pa=0.0, drive_kind=0, drive_p=0.02, drive_ns=4.0,
+                storage=0, launch=0, part_rank=0, part_world=0)
+
+
+def config(**overrides):
+    """A network configuration as a dict of the engine's field names."""
+    unknown = set(overrides) - set(DEFAULTS)
+    if unknown:
+        raise KeyError(sorted(unknown))
+    return dict(DEFAULTS, **overrides)
+
+
+# The benchmark workloads (sizes, distributions and drive of the benchmark configurations).
+def isolated_8k(seed=0):
+    return config(n=8192, n_exc=6553, topology=0, p_connect=0.02, weight_kind=0, w_mu=-2.0, w_sigma=0.5,
+                  seed=seed, drive_kind=0, drive_p=0.02, drive_ns=16.0)
+
+
+def scaled_262k(storage='csr', rate=0.03, seed=0):
+    n = 262144
+    common = dict(n=n, n_exc=int(n * 0.8), weight_kind=1, w_mu=0.0, w_sigma=0.05, seed=seed, drive_kind=1,
+                  drive_p=rate)
+    if storage == 'csr':
+        return config(topology=1, fanin=512, storage=0, **common)
+    return config(topology=2, bsr_blocks=128, bsr_fill=64, storage=1 if storage == 'bsr' else 0, **common)
+
+
+def partitioned_4m(rate=0.01, seed=0, scale=1):
+    n = 4194304 // scale
+    return config(n=n, n_exc=int(n * 0.8), topology=1, fanin=1000, weight_kind=1, w_mu=0.0, w_sigma=0.05,
+                  seed=seed, drive_kind=1, drive_p=rate)
+
+
+class TopoConfig(ct.Structure):
+    _fields_ = [('n', ct.c_int32), ('n_exc', ct.c_int32), ('topology', ct.c_int32), ('p_connect', ct.c_float),
+                ('fanin', ct.c_int32), ('bsr_blocks', ct.c_int32), ('bsr_fill', ct.c_int32),
+                ('weight_kind', ct.c_int32), ('w_mu', ct.c_float), ('w_sigma', ct.c_float),
+                ('delay_min', ct.c_int32), ('delay_max', ct.c_int32), ('seed', ct.c_uint64)]
+
+
+def _get(cfg, k):
+    return cfg[k] if isinstance(cfg, dict) else getattr(cfg, k)
+
+
+def generate(cfg, exact=False):
+    """Synapses of a generated network (oracle/net_topo.c, the engine's draws restated) ->
+    (pre, post, delay, weight fp32[, unrounded weight fp64]) in some fixed order."""
+    lib = ct.CDLL(str(HERE / 'liboracle.so'))
+    lib.ot_count.restype = ct.c_int64
+    lib.ot_count.argtypes = [ct.POINTER(TopoConfig)]
+    lib.ot_fill.argtypes = [ct.POINTER(TopoConfig)] + [ct.c_void_p] * 5
+    tc = TopoConfig(*[_get(cfg, k) for k, _ in TopoConfig._fields_])
+    m = lib.ot_count(ct.byref(tc))
+    pre, post, delay = (np.empty(m, np.int32) for _ in range(3))
+    w = np.empty(m, np.float32)
+    w64 = np.empty(m, np.float64) if exact else None
+    lib.ot_fill(ct.byref(tc), _p(pre), _p(post), _p(delay), _p(w), _p(w64))
+    return (pre, post, delay, w, w64) if exact else (pre, post, delay, w)
+
+
 class NetOracle:
-    def __init__(self, cfg, pre, post, delay, weight):
+    def __init__(self, cfg, pre, post, delay, weight, weight64=None):
+        """weight: the fp32-contract weights; weight64 (optional): the fp64 mode's weights
+        (default: the same values)."""
         lib = self.lib = ct.CDLL(str(HERE / 'liboracle.so'))
         lib.on_create.restype = ct.c_void_p
         lib.on_create.argtypes = [ct.POINTER(Params), ct.c_int64] + [ct.c_void_p] * 4
+        lib.on_create_w.restype = ct.c_void_p
+        lib.on_create_w.argtypes = [ct.POINTER(Params), ct.c_int64] + [ct.c_void_p] * 5
         lib.on_destroy.argtypes = [ct.c_void_p]
         lib.on_run.argtypes = [ct.c_void_p, ct.c_int, ct.c_void_p, ct.c_void_p]
         lib.on_run_mt.argtypes = [ct.c_void_p, ct.c_int, ct.c_void_p]
@@ -53,8 +123,9 @@ class NetOracle:
         self.n = self.params.n
         self.words = (self.n + 31) // 32
         self._keep = [np.ascontiguousarray(x, dt) for x, dt in
-                      ((pre, np.int32), (post, np.int32), (delay, np.int32), (weight, np.float64))]
-        self.h = lib.on_create(ct.byref(self.params), len(self._keep[0]), *[_p(x) for x in self._keep])
+                      ((pre, np.int32), (post, np.int32), (delay, np.int32), (weight, np.float32),
+                       (weight if weight64 is None else weight64, np.float64))]
+        self.h = lib.on_create_w(ct.byref(self.params), len(self._keep[0]), *[_p(x) for x in self._keep])
 
     def __del__(self):
         if getattr(self, 'h', None):

@@ -112,8 +112,22 @@ void on_destroy(void *h) {
 
 /* Edges in any order; stored by presynaptic neuron, stable in input order.
  * Weights are given in double; the fp32 mode uses them rounded to float. */
+/* Network from an edge list: fp32-contract weights w32 and, for the fp64
+ * mode, w64 (the same values, or the unrounded draws they were rounded from). */
+void *on_create_w(const on_params *p, int64_t nnz, const int32_t *pre, const int32_t *post,
+                  const int32_t *delay, const float *w32, const double *w64);
+
 void *on_create(const on_params *p, int64_t nnz, const int32_t *pre, const int32_t *post,
                 const int32_t *delay, const double *w) {
+  float *w32 = (float *)malloc((size_t)(nnz ? nnz : 1) * sizeof(float));
+  for (int64_t e = 0; e < nnz; ++e) w32[e] = (float)w[e];
+  void *o = on_create_w(p, nnz, pre, post, delay, w32, w);
+  free(w32);
+  return o;
+}
+
+void *on_create_w(const on_params *p, int64_t nnz, const int32_t *pre, const int32_t *post,
+                  const int32_t *delay, const float *w32, const double *w64) {
   on_net *o = (on_net *)calloc(1, sizeof(on_net));
   o->p = *p;
   int32_t n = p->n;
@@ -131,8 +145,8 @@ void *on_create(const on_params *p, int64_t nnz, const int32_t *pre, const int32
     int64_t k = fill[pre[e]]++;
     o->post[k] = post[e];
     o->delay[k] = delay[e];
-    o->w[k] = (float)w[e];
-    o->w64[k] = w[e];
+    o->w[k] = w32[e];
+    o->w64[k] = w64[e];
   }
   free(fill);
   size_t N = (size_t)n;

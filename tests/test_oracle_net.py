@@ -183,3 +183,65 @@ def test_scaled_configs_describe_the_benchmark():
     b = scaled_262k('bsr')
     assert (b.topology, b.bsr_blocks, b.bsr_fill, b.storage) == (2, 128, 64, 1)
     assert 128 * 64 // 16 == 512  # same mean fan-in as the CSR matrix
+
+
+def test_fp32_contract_raster_equals_fp64_unrounded_at_8k():
+    """The isolated 8,192-neuron benchmark network for its full 1,000 ticks: the engine's fp32
+    contract (weights rounded once onto the 2^-24 nS grid, fixed-point ring, polynomial exp)
+    against the fp64 equations with the unrounded lognormal weights and libm exp.  Every spike
+    decision of every tick agrees; the voltages stay within a few 1e-4 mV."""
+    from oracle import net as on
+    cfg = on.isolated_8k()
+    pre, post, delay, w, w64 = on.generate(cfg, exact=True)
+    # Half a grid step, plus fp32 rounding for weights above 0.5 nS.
+    assert (np.abs(w.astype(np.float64) - w64) <= 2.0 ** -25 + np.abs(w64) * 2.0 ** -24).all()
+    assert not np.array_equal(w.astype(np.float64), w64)   # the rounding did change weights
+    f32 = NetOracle(cfg, pre, post, delay, w)
+    f64 = NetOracle(cfg, pre, post, delay, w, w64)
+    T = 1000
+    s32, c32 = f32.run(T)
+    s64, v64, _, _ = f64.run64(T)
+    a, b = unpack_spikes(s32, cfg['n']), unpack_spikes(s64, cfg['n'])
+    mismatches = int((a != b).sum())
+    dv = float(np.abs(f32.get_state()['v'].astype(np.float64) - v64[-1]).max())
+    print(f'N=8,192, {T} ticks, {int(a.sum())} spikes: {mismatches} differing spike decisions; '
+          f'max |V32 - V64| after {T} ticks {dv:.2e} mV')
+    assert a.sum() > 100000 and mismatches == 0
+    assert dv < 1e-2
+
+
+@pytest.mark.parametrize('name', ['er', 'fanin', 'bsr'])
+def test_oracle_generator_equals_engine_generator(name):
+    """oracle/net_topo.c restates the engine's seeded generator: the same synapses (pre, post,
+    delay, weight bits), so the CPU legs build their networks without the CUDA library."""
+    from oracle import net as on
+    if name == 'er':
+        pc, oc = isolated_8k(seed=3), on.isolated_8k(seed=3)
+    elif name == 'fanin':
+        kw = dict(n=20000, n_exc=16000, topology=1, fanin=64, weight_kind=1, w_mu=0.0, w_sigma=0.05, seed=5,
+                  delay_min=2, delay_max=7)
+        pc, oc = default_config(**kw), on.config(**kw)
+    else:
+        kw = dict(n=4096, n_exc=3277, topology=2, bsr_blocks=32, bsr_fill=64, weight_kind=1, w_mu=0.0,
+                  w_sigma=0.05, seed=4)
+        pc, oc = default_config(**kw), on.config(**kw)
+
+    def canon(e):
+        pre, post, delay, w = e[:4]
+        o = np.lexsort((w.view(np.uint32), delay, post, pre))
+        return [x[o] for x in (pre, post, delay, w)]
+
+    for x, y in zip(canon(Topology(pc).export()), canon(on.generate(oc))):
+        assert np.array_equal(x, y)
+
+
+def test_oracle_workload_configs_equal_the_engines():
+    """The oracle-side workload definitions (used by the CPU legs) equal the engine's."""
+    from oracle import net as on
+    from neurogen_b200 import network as nw
+    pairs = [(nw.isolated_8k(seed=2), on.isolated_8k(seed=2)), (nw.scaled_262k('csr', 0.02), on.scaled_262k('csr', 0.02)),
+             (nw.scaled_262k('bsr', 0.03), on.scaled_262k('bsr', 0.03)), (nw.partitioned_4m(), on.partitioned_4m()),
+             (nw.default_config(), on.config())]
+    for eng, orc in pairs:
+        for k, v in orc.items():
+            assert getattr(eng, k) == (float(np.float32(v)) if isinstance(v, float) else v), k
