@@ -3,24 +3,27 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 Workloads (seeded synthetic inputs of the benchmark configurations):
-  tick262k  (default) scaled single-GPU tick: N=262,144, fan-in 512 CSR, fp16 weights, delays
+  tick262k  (headline) scaled single-GPU tick: N=262,144, fan-in 512 CSR, fp16 weights, delays
             1-8, imposed Bernoulli(0.03) spikes; one step = 10,000 ticks.  metric ticks/s.
   bsr262k   the same with the 16x16 block matrix (128 block-columns per block-row, 25% fill).
   tick8k    isolated tick: N=8,192 Erdos-Renyi 2%, lognormal fp32 weights, Bernoulli(0.02)
             conductance drive; one step = 1,000 ticks.  metric ticks/s.
-  partitioned4m  N=4,194,304, fan-in 1,000, fp16, imposed Bernoulli(0.01); under torchrun the
-            neurons are row-partitioned over the ranks with a per-tick NCCL all-gather of the
-            spike bitmask (one network: strong scaling); one step = 1,000 ticks.
+  partitioned4m  N=4,194,304, fan-in 1,000, fp16, imposed Bernoulli(0.01), 1,000 ticks a step;
+            under torchrun the neurons are row-partitioned over the ranks with a per-tick NCCL
+            all-gather of the spike bitmask (one network: strong scaling).
   bc250     BC-250 language core, seed-0 weights, batch 1, one step = 512 tokens.  tokens/s.
-  sessions  BC-250, 256 independent sessions (split over the ranks), one step = 64 tokens per
-            session.  tokens/s.
-Under torchrun every rank runs its share on its own GPU (tick workloads: independent replicas;
-sessions: a shard of the sessions); time is the max over ranks of CUDA-event time.
+  sessions  BC-250, 256 independent sessions (split over the ranks: strong scaling), one step =
+            64 tokens per session.  tokens/s.
+The line's top-level fields are the --workload (default tick262k); the other workloads follow
+under "workloads", each with its own value, roofline, e2e and (N=1) cpu_baseline.  Tick
+workloads other than partitioned4m do not shard (replicas: each rank runs its own seed).  With
+N>1 the line also carries "partition_parity": a 65,536-neuron network partitioned over the
+ranks, 100 ticks, compared on rank 0 with the same network run whole on one GPU.
 
---impl reference times the reference's own CPU implementation of the workload on this host's
-cores: the reference native library (oracle/_ref) for the language core, the C restatement of
-the reference simulator (oracle/net_oracle.c) for the tick network, which has no native
-implementation in the reference.
+--impl reference times the reference's own CPU implementation of each workload on this host's
+cores, with no CUDA library loaded: the reference native library (oracle/_ref) for the language
+core, the C restatement of the reference simulator (oracle/net_oracle.c, networks from
+oracle/net_topo.c) for the tick networks, which have no native implementation in the reference.
 """
 import argparse
 import json
@@ -40,6 +43,17 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 METRIC_TICKS = 'ticks/sec (synaptic events/sec alongside)'
 METRIC_TOKENS = 'tokens/sec at BC-250 profile'
+TICK_WORKLOADS = ('tick262k', 'bsr262k', 'tick8k', 'partitioned4m')
+LANG_WORKLOADS = ('bc250', 'sessions')
+WORKLOAD_NAMES = {'tick262k': 'scaled_tick_262144_csr', 'bsr262k': 'scaled_tick_262144_bsr16',
+                  'tick8k': 'isolated_tick_8192', 'partitioned4m': 'partitioned_4194304_fanin1000',
+                  'bc250': 'bc250_batch1', 'sessions': 'bc250_sessions256'}
+TICKS_PER_STEP = {'tick262k': 10000, 'bsr262k': 10000, 'tick8k': 1000, 'partitioned4m': 1000}
+TOKENS_PER_STEP = {'bc250': 512, 'sessions': 64}
+SESSIONS = 256
+# Steps and warm-up steps of the workloads that follow the headline (bounded run time).
+EXTRA_STEPS = {'tick262k': 3, 'bsr262k': 3, 'tick8k': 10, 'partitioned4m': 3, 'bc250': 3, 'sessions': 5}
+L2_BYTES = 126e6
 
 
 def parse():
@@ -47,12 +61,12 @@ def parse():
     p.add_argument('--gpus', type=int, default=1)
     p.add_argument('--steps', type=int, default=5)
     p.add_argument('--warmup', type=int, default=3)
-    p.add_argument('--workload', default='tick262k',
-                   choices=['tick262k', 'bsr262k', 'tick8k', 'partitioned4m', 'bc250', 'sessions'])
+    p.add_argument('--workload', default='tick262k', choices=list(TICK_WORKLOADS + LANG_WORKLOADS))
     p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     p.add_argument('--rate', type=float, default=0.03)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--no-extras', action='store_true', help='time the --workload only')
     p.add_argument('--ticks', type=int, default=0, help='override ticks per step (profiling runs)')
     p.add_argument('--tokens', type=int, default=0, help='override tokens per step (profiling runs)')
     p.add_argument('--neurons', type=int, default=0,
@@ -65,8 +79,7 @@ def parse():
 def peaks():
     path = ROOT / 'MEASURED_PEAKS.json'
     if path.is_file():
-        d = json.loads(path.read_text())
-        return d, 'measured'
+        return json.loads(path.read_text()), 'measured'
     return dict(PEAKS_FALLBACK), 'fallback'
 
 
@@ -77,12 +90,12 @@ class Dist:
         self.local = int(os.environ.get('LOCAL_RANK', '0'))
         self.pg = None
 
-    def init(self, device):
+    def init(self):
         import torch
         if self.world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+            dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device('cuda', self.local))
             self.pg = dist
 
@@ -90,21 +103,19 @@ class Dist:
         if self.pg:
             self.pg.barrier()
 
-    def max(self, x):
+    def _reduce(self, x, op):
         if not self.pg:
             return x
         import torch
         t = torch.tensor([x], dtype=torch.float64, device='cuda')
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        self.pg.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, x):
+        return self._reduce(x, self.pg.ReduceOp.MAX) if self.pg else x
+
     def sum(self, x):
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64, device='cuda')
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
+        return self._reduce(x, self.pg.ReduceOp.SUM) if self.pg else x
 
     def close(self):
         if self.pg:
@@ -112,7 +123,7 @@ class Dist:
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling during a timed region."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
@@ -158,31 +169,88 @@ class Clocks:
                 'reasons': reasons, 'samples': len(rows)}
 
 
-def cuda_timer(fn, stream):
+class L2Flush:
+    """Writes a buffer twice the size of L2 between timed steps (outside the timed region)."""
+
+    def __init__(self):
+        import torch
+        self.buf = torch.empty(int(2 * L2_BYTES) // 4, dtype=torch.int32, device='cuda')
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def time_steps(step, stream, steps, flush=None):
+    """CUDA-event time of `steps` calls of step() on `stream`, each bracketed by a device
+    synchronisation; the L2 flush (if any) runs between steps, outside the timed region."""
     import torch
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    start.record(stream)
-    fn()
-    end.record(stream)
-    torch.cuda.synchronize()
-    return start.elapsed_time(end) / 1e3
+    total = 0.0
+    for _ in range(steps):
+        if flush:
+            flush()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        total += start.elapsed_time(end) / 1e3
+    return total
 
 
 # ---------------------------------------------------------------------------
-# Tick-network workloads.
+# Workload definitions shared by both arms.
 # ---------------------------------------------------------------------------
-def tick_config(name, rate, rank=0, world=1):
-    from neurogen_b200.network import scaled_262k, isolated_8k, partitioned_4m
+def oracle_tick_config(name, rate, n_override=0):
+    """The workload's network configuration as the oracle's dict (no CUDA library)."""
+    from oracle import net as on
     if name == 'partitioned4m':
-        return partitioned_4m(rank, world, rate=0.01), 1000, 'partitioned_4194304_fanin1000'
+        c = on.partitioned_4m(rate=0.01)
+        if n_override:
+            c.update(n=n_override, n_exc=int(n_override * 0.8))
+        return c
     if name == 'tick262k':
-        return scaled_262k('csr', rate=rate), 10000, 'scaled_tick_262144_csr'
+        return on.scaled_262k('csr', rate=rate)
     if name == 'bsr262k':
-        return scaled_262k('bsr', rate=rate), 10000, 'scaled_tick_262144_bsr16'
-    return isolated_8k(), 1000, 'isolated_tick_8192'
+        return on.scaled_262k('bsr', rate=rate)
+    return on.isolated_8k()
 
 
+def tick_config_dict(name, c, world, ticks):
+    """The `config` object of a tick workload: what the workload is, identical in both arms."""
+    fanin, topo = c['fanin'], c['topology']
+    synapses = (c['n'] * fanin if topo == 1 else
+                (c['n'] // 16) * c['bsr_blocks'] * c['bsr_fill'] if topo == 2 else
+                round(c['n'] * (c['n'] - 1) * c['p_connect']))
+    part = name == 'partitioned4m'
+    return {'workload': WORKLOAD_NAMES[name], 'n': c['n'], 'ticks_per_step': ticks,
+            'fanin': fanin if topo == 1 else None,
+            'bsr': [c['bsr_blocks'], c['bsr_fill']] if topo == 2 else None,
+            'drive': ('imposed Bernoulli(%g) spikes' % c['drive_p'] if c['drive_kind'] == 1 else
+                      'Bernoulli(%g) conductance drive of %g nS' % (c['drive_p'], c['drive_ns'])),
+            'weights': 'fp16' if c['weight_kind'] == 1 else 'fp32', 'delays': [c['delay_min'], c['delay_max']],
+            'synapses': synapses if topo != 0 else f'~{synapses}',
+            'l2': 'inputs larger than L2' if synapses * 6 > L2_BYTES else 'network fits in L2; L2 flushed between steps',
+            'parallelism': (f'rows{world} + NCCL bitmask all-gather' if part and world > 1 else
+                            'one GPU' if part else f'replicas{world}')}
+
+
+def lang_config_dict(name, world, sessions=SESSIONS):
+    return {'workload': WORKLOAD_NAMES[name], 'sessions': 1 if name == 'bc250' else sessions,
+            'tokens_per_step': TOKENS_PER_STEP[name], 'weights': 'seed-0 random init (packed 14,804,744 fp32)',
+            'l2': 'weights (59 MB) L2-resident by design; L2 flushed between steps',
+            'parallelism': f'replicas{world}' if name == 'bc250' else f'dp{world} over sessions'}
+
+
+def engine_config(c):
+    """The engine's NetConfig from an oracle config dict."""
+    from neurogen_b200.network import default_config
+    return default_config(**{k: v for k, v in c.items()})
+
+
+# ---------------------------------------------------------------------------
+# Tick-network workloads (our arm).
+# ---------------------------------------------------------------------------
 def tick_bytes(cfg, spikes, events, held=None):
     """Algorithmic DRAM bytes of one tick, the roofline numerator.
 
@@ -223,56 +291,59 @@ def tick_launches(mode, ticks):
     """Kernels the engine launches for one run of `ticks` ticks without per-tick outputs."""
     if mode == 'resident':
         return -(-ticks // 2048)
-    per_tick = 1 if mode == 'fused' else (3 if mode == 'split' else 1)
+    per_tick = 1 if mode == 'fused' else 3
     graphs = ticks // 64
     return graphs * (64 * per_tick + 1) + (ticks - graphs * 64) * per_tick + (1 if graphs else 0)
 
 
-def bench_ticks(args, dist):
+def bench_ticks(name, args, dist, steps, warmup, cpu=True):
     import torch
     from neurogen_b200 import library
     from neurogen_b200.network import Topology, Network, nccl_unique_id
     lib = library()
-    part = args.workload == 'partitioned4m'
-    cfg, ticks, wl = tick_config(args.workload, args.rate, dist.rank, dist.world)
-    ticks = args.ticks or ticks
-    if part and args.neurons:
-        cfg.n, cfg.n_exc = args.neurons, int(args.neurons * 0.8)
-    if not part:
+    part = name == 'partitioned4m'
+    rate = args.rate
+    ticks = args.ticks or TICKS_PER_STEP[name]
+    oc = oracle_tick_config(name, rate, args.neurons if part else 0)
+    cfg = engine_config(oc)
+    if part:
+        cfg.part_rank, cfg.part_world = dist.rank, (dist.world if dist.world > 1 else 0)
+    else:
         cfg.seed = cfg.seed + dist.rank  # independent replica per rank
     t0 = time.time()
-    if part and dist.world > 1:
-        ids = [nccl_unique_id() if dist.rank == 0 else None]
-        dist.pg.broadcast_object_list(ids, src=0)
-        net = Network.partitioned(cfg, ids[0])
-        synapses = net.synapses * dist.world
+    if part:
+        if dist.world > 1:
+            ids = [nccl_unique_id() if dist.rank == 0 else None]
+            dist.pg.broadcast_object_list(ids, src=0)
+            net = Network.partitioned(cfg, ids[0])
+        else:
+            net = Network(cfg)
+        synapses = int(dist.sum(net.synapses))
     else:
-        topo = Topology(cfg)
-        net = topo.network()
-        synapses = topo.synapses
+        topo = Topology(cfg) if cfg.topology != 1 or cfg.weight_kind != 1 else None
+        net = topo.network() if topo else Network(cfg)   # fixed fan-in fp16: drawn on the device
+        synapses = net.synapses
     setup_s = time.time() - t0
-    mode = net.launch  # 'fused', 'split' or 'resident'
+    mode = net.launch
     stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
         if lib.ng_net_run_device(net.h, ticks, None, None, stream.cuda_stream):
             raise RuntimeError(lib.ng_error().decode())
 
-    for _ in range(args.warmup):
+    flush = L2Flush() if synapses * 6 < L2_BYTES else None
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
     s0, e0 = net.stats()
     with Clocks(torch.cuda.current_device()) as clk:
-        elapsed = 0.0
-        for _ in range(args.steps):
-            elapsed += cuda_timer(step, stream)
+        elapsed = time_steps(step, stream, steps, flush)
     s1, e1 = net.stats()
     spikes, events = s1 - s0, e1 - e0
     dist.barrier()
     t_max = dist.max(elapsed)
-    total_ticks = ticks * args.steps
-    per_tick_s = elapsed / total_ticks
+    total_ticks = ticks * steps
     held = cfg.n // dist.world if part else cfg.n
     b_tick = tick_bytes(cfg, spikes / total_ticks, events / total_ticks, held)
     pk, src = peaks()
@@ -281,38 +352,32 @@ def bench_ticks(args, dist):
         spikes, events = dist.sum(spikes), dist.sum(events)
     achieved = b_tick / (t_max / total_ticks) / 1e9
     peak_total = pk['hbm_gbs'] * (dist.world if part else 1)
-    line = {
+    rec = {
         'metric': METRIC_TICKS, 'value': total_ticks * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
-        'n_gpus': dist.world, 'steps': args.steps, 'warmup': args.warmup,
-        'ms_per_step': t_max / args.steps * 1e3, 'higher_is_better': True,
-        'scaling': 'strong' if part else 'weak',
-        'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic',
-        'config': {'workload': wl, 'n': cfg.n, 'ticks_per_step': ticks,
-                   'fanin': cfg.fanin if cfg.topology == 1 else None,
-                   'bsr': [cfg.bsr_blocks, cfg.bsr_fill] if cfg.topology == 2 else None,
-                   'spike_rate': spikes / total_ticks / cfg.n, 'weights': 'fp16' if cfg.weight_kind else 'fp32',
-                   'delays': [cfg.delay_min, cfg.delay_max], 'synapses': synapses,
-                   'l2': 'inputs larger than L2' if synapses * 6 > 126e6 else 'network fits in L2',
-                   'parallelism': (f'rows{dist.world} + NCCL bitmask all-gather' if part and dist.world > 1
-                                   else f'replicas{dist.world}'),
-                   'launch': mode, 'setup_s': round(setup_s, 2)},
+        'n_gpus': dist.world, 'steps': steps, 'warmup': warmup, 'ms_per_step': t_max / steps * 1e3,
+        'higher_is_better': True, 'scaling': 'strong' if part else 'weak', 'vs_baseline': None,
+        'dtype': 'fp32', 'data': 'synthetic', 'config': tick_config_dict(name, oc, dist.world, ticks),
+        'measured': {'spike_rate': spikes / total_ticks / cfg.n, 'events_per_tick': events / total_ticks,
+                     'launch': mode, 'setup_s': round(setup_s, 2)},
         'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
                      'frac': achieved / peak_total,
-                     'traffic': tick_traffic(wl, mode, spikes / total_ticks / cfg.n) if not part else None,
+                     'traffic': (tick_traffic(WORKLOAD_NAMES[name], mode, spikes / total_ticks / cfg.n)
+                                 if not part else None),
                      'traffic_unit': 'bytes/tick (ncu, scaled by spike rate)', 'bytes_per_tick': b_tick,
                      'kernel': KERNEL_OF_LAUNCH[mode], 'peak_source': src},
-        'gpu_launches': tick_launches(mode, ticks) * args.steps,
+        'gpu_launches': tick_launches(mode, ticks) * steps,
         'clocks': clk.summary(),
     }
     if not args.no_e2e:
-        line['e2e'] = e2e_ticks(args, lib, net, cfg, ticks, dist, part)
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and not part:
-        line['cpu_baseline'] = cpu_baseline_ticks(cfg, topo)
-    return line
+        rec['e2e'] = e2e_ticks(lib, net, ticks, steps, warmup, dist, part)
+    if cpu and dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        rec['cpu_baseline'] = cpu_baseline_ticks(name, oc, budget_s=12.0 if name == 'tick262k' else 6.0)
+    net.close()
+    return rec
 
 
-def e2e_ticks(args, lib, net, cfg, ticks, dist, part=False):
+def e2e_ticks(lib, net, ticks, steps, warmup, dist, part=False):
     """Through the C ABI with host buffers: per step, upload the full network state from
     pinned host memory, run the ticks, read back the spike/event totals and the state."""
     import ctypes as ct
@@ -338,44 +403,52 @@ def e2e_ticks(args, lib, net, cfg, ticks, dist, part=False):
             raise RuntimeError(lib.ng_error().decode())
         return time.perf_counter() - t0
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         step()
     dist.barrier()
-    elapsed = sum(step() for _ in range(args.steps))
+    elapsed = sum(step() for _ in range(steps))
     t_max = dist.max(elapsed)
-    return {'value': ticks * args.steps * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
+    return {'value': ticks * steps * (1 if part else dist.world) / t_max, 'unit': 'ticks/s',
             'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
             'api': 'ng_net_set_state + ng_net_run + ng_net_stats + ng_net_get_state (host buffers)'}
 
 
-def cpu_baseline_ticks(cfg, topo, budget_s=12.0):
-    from oracle.net import NetOracle
+def oracle_network(name, oc):
+    """(oracle, scale): the workload's network on the CPU checker; partitioned4m at 1/16 of its
+    neurons (same fan-in and rate; 4.2 billion synapses do not fit a host-side checker)."""
+    from oracle import net as on
+    scale = 1
+    if name == 'partitioned4m':
+        scale = 16
+        oc = dict(oc, n=oc['n'] // scale, n_exc=oc['n_exc'] // scale)
+    return on.NetOracle(oc, *on.generate(oc)), scale
+
+
+def cpu_baseline_ticks(name, oc, budget_s):
     import multiprocessing
     t0 = time.time()
-    orc = NetOracle(cfg, *topo.export())
+    orc, scale = oracle_network(name, oc)
     build_s = time.time() - t0
     orc.run_mt(2)
     done, el = 0, 0.0
-    chunk = 5 if cfg.n > 100000 else 200
+    chunk = 5 if oc['n'] > 100000 else 100
     while el < budget_s:
         t1 = time.time()
         orc.run_mt(chunk)
         el += time.time() - t1
         done += chunk
     cores = int(os.environ.get('OMP_NUM_THREADS', multiprocessing.cpu_count()))
-    return {'value': done / el, 'unit': 'ticks/s', 'cores': cores, 'kind': 'port',
-            'sample': f'{done} ticks of the same network (oracle/net_oracle.c on_run_mt, OpenMP), '
-                      f'{el:.1f} s; oracle build {build_s:.1f} s excluded'}
+    sample = (f'{done} ticks of the same network (oracle/net_oracle.c on_run_mt, OpenMP), {el:.1f} s; '
+              f'network generation {build_s:.1f} s excluded')
+    if scale > 1:
+        sample += f'; 1/{scale}-scale network, time per tick x{scale}'
+    return {'value': done / el / scale, 'unit': 'ticks/s', 'cores': cores, 'kind': 'port', 'sample': sample}
 
 
 # ---------------------------------------------------------------------------
-# Language-core workloads.
+# Language-core workloads (our arm).
 # ---------------------------------------------------------------------------
-LANG_TOKENS_PER_STEP = {'bc250': 512, 'sessions': 64}
-SESSIONS = 256
-
-
-def lang_tokens(workload, sessions, steps_tokens, seed_base=0):
+def lang_tokens(workload, sessions, steps_tokens):
     import torch
     if workload == 'bc250':
         g = torch.Generator().manual_seed(0)
@@ -413,7 +486,7 @@ def lang_launches_per_token(cfg):
     return per + 2
 
 
-def bench_lang(args, dist):
+def bench_lang(name, args, dist, steps, warmup, cpu=True):
     import torch
     from neurogen_b200 import library
     from neurogen_b200.language import LanguageConfig, NativeEngine, init_packed_weights
@@ -421,14 +494,15 @@ def bench_lang(args, dist):
     cfg = LanguageConfig()
     w = init_packed_weights(cfg, seed=0)
     eng = NativeEngine(cfg, w)
-    if args.workload == 'bc250':
+    n_sessions = args.sessions or SESSIONS
+    if name == 'bc250':
         mine = [0]
     else:
-        per = (args.sessions or SESSIONS) // dist.world
+        per = n_sessions // dist.world
         mine = list(range(dist.rank * per, (dist.rank + 1) * per))
     B = len(mine)
-    T = args.tokens or LANG_TOKENS_PER_STEP[args.workload]
-    toks = lang_tokens(args.workload, mine, 1024 if args.workload == 'sessions' else 512)
+    T = args.tokens or TOKENS_PER_STEP[name]
+    toks = lang_tokens(name, mine, 1024 if name == 'sessions' else 512)
     pool = lib.ng_pool_create(eng.handle, B)
     if not pool:
         raise RuntimeError(lib.ng_error().decode())
@@ -444,31 +518,32 @@ def bench_lang(args, dist):
                 raise RuntimeError(lib.ng_error().decode())
             pos[0] += 1
 
-    for _ in range(args.warmup):
+    flush = L2Flush()
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
     with Clocks(torch.cuda.current_device()) as clk:
-        elapsed = sum(cuda_timer(step, stream) for _ in range(args.steps))
+        elapsed = time_steps(step, stream, steps, flush)
     dist.barrier()
     t_max = dist.max(elapsed)
-    total = B * T * args.steps * dist.world
+    total = B * T * steps * (dist.world if name == 'sessions' else dist.world)
     fl = lang_flops_per_token(cfg)
     pk, src = peaks()
-    achieved = fl * B * T * args.steps / elapsed / 1e12
-    line = {
+    achieved = fl * B * T * steps / elapsed / 1e12
+    rec = {
         'metric': METRIC_TOKENS, 'value': total / t_max, 'unit': 'tokens/s', 'n_gpus': dist.world,
-        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': t_max / args.steps * 1e3,
-        'higher_is_better': True, 'scaling': 'strong' if args.workload == 'sessions' else 'weak',
+        'steps': steps, 'warmup': warmup, 'ms_per_step': t_max / steps * 1e3,
+        'higher_is_better': True, 'scaling': 'strong' if name == 'sessions' else 'weak',
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic',
-        'config': {'workload': 'bc250_batch1' if args.workload == 'bc250' else 'bc250_sessions256',
-                   'sessions': (args.sessions or SESSIONS) if args.workload == 'sessions' else 1, 'tokens_per_step': T,
-                   'sessions_per_gpu': B, 'weights': 'seed-0 random init (packed 14,804,744 fp32)',
-                   'l2': 'weights (59 MB) L2-resident by design', 'parallelism': f'dp{dist.world}'},
+        'config': lang_config_dict(name, dist.world, n_sessions),
+        'measured': {'sessions_per_gpu': B, 'tokens_per_step': T},
         'roofline': {'bound': 'tensor', 'achieved': achieved, 'peak': pk.get('bf16_tflops'),
                      'unit': 'TFLOP/s', 'frac': achieved / pk.get('bf16_tflops'), 'traffic': None,
-                     'note': 'exact fp32 SIMT path; FLOPs per token 2x MACs', 'peak_source': src},
-        'gpu_launches': lang_launches_per_token(cfg) * T * args.steps,
+                     'note': 'exact fp32 SIMT path (bit-exact with the reference); FLOPs per token 2x MACs; '
+                             'a small fraction of the bf16 tensor peak by construction',
+                     'peak_source': src},
+        'gpu_launches': lang_launches_per_token(cfg) * T * steps,
         'clocks': clk.summary(),
     }
     if not args.no_e2e:
@@ -485,103 +560,145 @@ def bench_lang(args, dist):
             return time.perf_counter() - t0
         e2e_step()
         dist.barrier()
-        el = dist.max(sum(e2e_step() for _ in range(args.steps)))
-        line['e2e'] = {'value': total / el, 'unit': 'tokens/s', 'h2d_bytes_per_step': B * 4 * T,
-                       'd2h_bytes_per_step': B * 264 * 4 * T, 'api': 'ng_pool_step (host tokens, host logits)'}
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line['cpu_baseline'] = cpu_baseline_lang(cfg, w, toks)
+        el = dist.max(sum(e2e_step() for _ in range(steps)))
+        rec['e2e'] = {'value': total / el, 'unit': 'tokens/s', 'h2d_bytes_per_step': B * 4 * T,
+                      'd2h_bytes_per_step': B * 264 * 4 * T, 'api': 'ng_pool_step (host tokens, host logits)'}
+    if cpu and dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        rec['cpu_baseline'] = cpu_baseline_lang(name, toks, budget_s=8.0)
     lib.ng_pool_destroy(pool)
-    return line
+    eng.close()
+    return rec
 
 
-def cpu_baseline_lang(cfg, w, toks, budget_s=10.0):
-    from oracle.lang import RefEngine
-    ref = RefEngine(cfg, w)
-    s = np.zeros(ref.S, np.float32)
-    n, t0 = 0, time.time()
-    while time.time() - t0 < budget_s:
-        _, s, _, _ = ref.step(int(toks[n % len(toks), 0]), s)
-        n += 1
+def cpu_baseline_lang(name, toks, budget_s):
+    """The reference native library (oracle/_ref): batch 1 on one thread; the sessions workload on
+    every host core, one engine per thread, each serving its own sessions."""
+    import multiprocessing
+    from concurrent.futures import ThreadPoolExecutor
+    from neurogen_b200.language import LanguageConfig
+    from oracle.lang import RefEngine, seeded_weights
+    cfg = LanguageConfig()
+    w = seeded_weights()
+    threads = 1 if name == 'bc250' else multiprocessing.cpu_count()
+    engines = [RefEngine(cfg, w) for _ in range(threads)]
+    states = [np.zeros(engines[0].S, np.float32) for _ in range(threads)]
+    counts = [0] * threads
+    stop = time.time() + budget_s
+
+    def work(k):
+        i = 0
+        while time.time() < stop:
+            _, states[k], _, _ = engines[k].step(int(toks[i % len(toks), k % toks.shape[1]]), states[k])
+            i += 1
+        counts[k] = i
+
+    t0 = time.time()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(work, range(threads)))
     el = time.time() - t0
-    return {'value': n / el, 'unit': 'tokens/s', 'cores': 1, 'kind': 'reference',
-            'sample': f'{n} tokens, one session, reference native CPU library (oracle/_ref), 1 thread'}
+    return {'value': sum(counts) / el, 'unit': 'tokens/s', 'cores': threads, 'kind': 'reference',
+            'sample': f'{sum(counts)} tokens in {el:.1f} s on {threads} thread(s), one engine and session each, '
+                      'reference native CPU library (oracle/_ref)'}
 
 
 # ---------------------------------------------------------------------------
-# Reference arm.
+# Partition parity (N > 1).
 # ---------------------------------------------------------------------------
-def reference_arm(args):
+def partition_parity(dist):
+    """A 65,536-neuron network (fan-in 96, self-generated spikes) row-partitioned over the ranks:
+    100 ticks, every rank recording the whole network's raster; rank 0 runs the same network whole
+    on its own GPU and compares rasters, per-tick counts and totals."""
+    import torch
+    from neurogen_b200.network import Network, default_config, nccl_unique_id
+    kw = dict(n=65536, n_exc=52428, topology='fixed_fanin', fanin=96, weight_kind='halfnormal_f16', w_mu=0.0,
+              w_sigma=0.05, drive_kind='conductance', drive_p=0.03, drive_ns=18.0, seed=12)
+    ids = [nccl_unique_id() if dist.rank == 0 else None]
+    dist.pg.broadcast_object_list(ids, src=0)
+    net = Network.partitioned(default_config(part_rank=dist.rank, part_world=dist.world, **kw), ids[0])
+    spikes, counts = net.run(100)
+    mine = np.array(net.stats(), np.float64)
+    tot = torch.from_numpy(mine).cuda()
+    dist.pg.all_reduce(tot)
+    net.close()
+    ok = True
+    detail = {}
+    if dist.rank == 0:
+        full = Network(default_config(**kw))
+        fs, fc = full.run(100)
+        ok = (np.array_equal(spikes, fs) and np.array_equal(counts[:, 0], fc[:, 0]) and
+              tuple(int(x) for x in tot.cpu().numpy()) == full.stats())
+        detail = {'ticks': 100, 'n': kw['n'], 'spikes': int(fc[:, 0].sum()), 'ranks': dist.world}
+        full.close()
+    flag = torch.tensor([1.0 if ok else 0.0], device='cuda')
+    dist.pg.all_reduce(flag, op=dist.pg.ReduceOp.MIN)
+    return dict(result='pass' if flag.item() == 1.0 else 'fail', **detail)
+
+
+# ---------------------------------------------------------------------------
+# Reference arm (CPU; no CUDA library).
+# ---------------------------------------------------------------------------
+def reference_record(name, args, world, steps, warmup):
     import multiprocessing
     cores = multiprocessing.cpu_count()
-    if args.workload in ('tick262k', 'bsr262k', 'tick8k', 'partitioned4m'):
-        from neurogen_b200.network import Topology
-        from oracle.net import NetOracle
-        cfg, ticks, wl = tick_config(args.workload, args.rate)
-        scale = 1
-        if args.workload == 'partitioned4m':
-            # 4.2 billion synapses do not fit a host-side checker: run 1/16 of the neurons with
-            # the same fan-in and rate, and scale the time per tick by 16 (work per tick is
-            # proportional to the neuron count).
-            scale = 16
-            cfg.n //= scale
-            cfg.n_exc //= scale
-        orc = NetOracle(cfg, *Topology(cfg).export())
-        sample = 20 if cfg.n > 100000 else 200
-        for _ in range(args.warmup):
+    if name in TICK_WORKLOADS:
+        oc = oracle_tick_config(name, args.rate)
+        orc, scale = oracle_network(name, oc)
+        sample = 20 if oc['n'] > 100000 else 200
+        for _ in range(warmup):
             orc.run_mt(sample)
         t0 = time.time()
-        for _ in range(args.steps):
+        for _ in range(steps):
             orc.run_mt(sample)
         el = time.time() - t0
-        value, unit = sample * args.steps / el / scale, 'ticks/s'
-        ms_per_step = el / args.steps * 1e3 * scale
-        config = {'workload': wl, 'n': cfg.n * scale, 'ticks_per_step': sample,
-                  'fanin': cfg.fanin if cfg.topology == 1 else None,
-                  'bsr': [cfg.bsr_blocks, cfg.bsr_fill] if cfg.topology == 2 else None,
-                  'spike_rate': args.rate if cfg.drive_kind == 1 else None,
-                  'weights': 'fp16' if cfg.weight_kind else 'fp32', 'delays': [cfg.delay_min, cfg.delay_max]}
-        scaling = 'strong' if args.workload == 'partitioned4m' else 'weak'
-        kind, desc = 'port', f'{sample} ticks per step of {wl} (oracle/net_oracle.c, OpenMP)'
+        value, unit = sample * steps / el / scale, 'ticks/s'
+        ms_per_step = el / steps * 1e3 * scale / sample * TICKS_PER_STEP[name]
+        config = tick_config_dict(name, oc, world, TICKS_PER_STEP[name])
+        scaling = 'strong' if name == 'partitioned4m' else 'weak'
+        kind, threads = 'port', cores
+        desc = f'{sample} ticks per step (oracle/net_oracle.c, OpenMP on {cores} cores)'
         if scale > 1:
-            desc += f'; 1/{scale}-scale network (N={cfg.n:,}), time per tick x{scale}'
+            desc += f'; 1/{scale}-scale network (N={oc["n"] // scale:,}), time per tick x{scale}'
         metric = METRIC_TICKS
     else:
-        from neurogen_b200.language import LanguageConfig, init_packed_weights
-        from oracle.lang import RefEngine
         from concurrent.futures import ThreadPoolExecutor
-        cfg = LanguageConfig()
-        w = init_packed_weights(cfg, seed=0)
-        wl = 'bc250_batch1' if args.workload == 'bc250' else 'bc250_sessions256'
-        threads = 1 if args.workload == 'bc250' else cores
-        engines = [RefEngine(cfg, w) for _ in range(threads)]
+        from oracle.lang import RefEngine, seeded_weights
+
+        class Cfg:
+            columns, width, regions, ticks, idle_steps = 32, 768, 4, 2, 1
+        w = seeded_weights()
+        threads = 1 if name == 'bc250' else cores
+        engines = [RefEngine(Cfg, w) for _ in range(threads)]
         states = [np.zeros(engines[0].S, np.float32) for _ in range(threads)]
-        per_step = 8 if args.workload == 'bc250' else 2
+        per_step = 8 if name == 'bc250' else 2
 
         def work(k):
             for i in range(per_step):
                 _, states[k], _, _ = engines[k].step((k * 7 + i) % 264, states[k])
 
-        with ThreadPoolExecutor(threads) as pool:
-            for _ in range(args.warmup):
-                list(pool.map(work, range(threads)))
+        with ThreadPoolExecutor(threads) as ex:
+            for _ in range(warmup):
+                list(ex.map(work, range(threads)))
             t0 = time.time()
-            for _ in range(args.steps):
-                list(pool.map(work, range(threads)))
+            for _ in range(steps):
+                list(ex.map(work, range(threads)))
             el = time.time() - t0
-        value, unit = threads * per_step * args.steps / el, 'tokens/s'
-        ms_per_step = el / args.steps * 1e3
-        config = {'workload': wl, 'sessions': 1 if args.workload == 'bc250' else SESSIONS,
-                  'tokens_per_step': per_step * threads}
-        scaling = 'weak' if args.workload == 'bc250' else 'strong'
+        value, unit = threads * per_step * steps / el, 'tokens/s'
+        ms_per_step = el / steps * 1e3
+        config = lang_config_dict(name, world)
+        scaling = 'weak' if name == 'bc250' else 'strong'
         kind = 'reference'
         desc = f'{per_step} tokens per step on each of {threads} independent sessions (one engine per thread)'
+        sample = per_step * threads
         metric = METRIC_TOKENS
-    return {'metric': metric, 'value': value, 'unit': unit, 'n_gpus': int(os.environ.get('WORLD_SIZE', '1')),
-            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
-            'scaling': scaling, 'impl': 'reference', 'dtype': 'fp32', 'data': 'synthetic', 'config': config,
-            'cpu_baseline': {'value': value, 'unit': unit, 'cores': cores if kind == 'port' or threads > 1 else 1,
-                             'kind': kind, 'sample': desc},
+    return {'metric': metric, 'value': value, 'unit': unit, 'n_gpus': world, 'steps': steps, 'warmup': warmup,
+            'ms_per_step': ms_per_step, 'higher_is_better': True, 'scaling': scaling, 'impl': 'reference',
+            'dtype': 'fp32', 'data': 'synthetic', 'config': config, 'sample_per_step': sample,
+            'cpu_baseline': {'value': value, 'unit': unit, 'cores': threads, 'kind': kind, 'sample': desc},
             'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+
+
+def extras_for(headline):
+    return [w for w in ('bc250', 'sessions', 'tick8k', 'bsr262k', 'partitioned4m') if w != headline]
 
 
 def main():
@@ -589,16 +706,28 @@ def main():
     dist = Dist()
     if args.impl == 'reference':
         if dist.rank == 0:
-            print(json.dumps(reference_arm(args)), flush=True)
+            line = reference_record(args.workload, args, dist.world, args.steps, args.warmup)
+            if not args.no_extras:
+                line['workloads'] = {WORKLOAD_NAMES[w]: reference_record(w, args, dist.world, 3, 1)
+                                     for w in extras_for(args.workload)}
+            print(json.dumps(line), flush=True)
         return
     import torch
     torch.cuda.set_device(dist.local)
-    dist.init(dist.local)
+    dist.init()
+    run = lambda w, steps, warmup, cpu=True: (bench_lang if w in LANG_WORKLOADS else bench_ticks)(
+        w, args, dist, steps, warmup, cpu)
     try:
-        if args.workload in ('bc250', 'sessions'):
-            line = bench_lang(args, dist)
-        else:
-            line = bench_ticks(args, dist)
+        line = run(args.workload, args.steps, args.warmup)
+        if not args.no_extras:
+            line['workloads'] = {}
+            for w in extras_for(args.workload):
+                rec = run(w, EXTRA_STEPS[w], 3)
+                line['workloads'][WORKLOAD_NAMES[w]] = rec
+                line['gpu_launches_all_workloads'] = line.get('gpu_launches_all_workloads',
+                                                              line['gpu_launches']) + rec['gpu_launches']
+        if dist.world > 1:
+            line['partition_parity'] = partition_parity(dist)
         if dist.rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -139,3 +139,26 @@ def last_spikes(state, config):
     n, w = config.columns * 64, config.width
     rs = 5 * n + w
     return np.stack([state[..., r * rs + 3 * n: r * rs + 4 * n] for r in range(config.regions)], -2)
+
+
+def seeded_weights(columns=32, width=768, regions=4, seed=0):
+    """Packed weights of the reference ``LanguageModel`` after ``torch.manual_seed(seed)``, for the
+    CPU legs (no CUDA library).  The parameters the native stream holds are drawn with the same
+    torch modules in the construction order of neurogen/language/model.py:103-116 (embedding with
+    its padding row zeroed, then per region input / feedback / output Linear layers, then the
+    head); constant-initialised parameters draw nothing.  Pinned by the SHA-256 of the seed-0
+    BC-250 stream in tests/golden/lang_golden.npz."""
+    import torch
+    c, w = columns, width
+    with torch.random.fork_rng(devices=[]):
+        torch.manual_seed(seed)
+        parts = [torch.nn.Embedding(VOCAB, w, padding_idx=256).weight]
+        for _ in range(regions):
+            inp = torch.nn.Linear(w, c * 12)
+            fb = torch.nn.Linear(w, c * 29, bias=False)
+            out = torch.nn.Linear(c * 100, w)
+            parts += [torch.full((c, 64, 64), -1.8), inp.weight, inp.bias, fb.weight, out.weight, out.bias,
+                      torch.ones(w), torch.zeros(w), torch.full((w,), 2.9)]
+        head = torch.nn.Linear(w, VOCAB)
+        parts += [head.weight, head.bias]
+        return np.concatenate([p.detach().float().numpy().reshape(-1) for p in parts]).astype(np.float32)

@@ -110,3 +110,13 @@ def test_spike_recording_agrees_with_state(golden_lang):
             assert np.array_equal(counts - before, per[:, r].sum((0, 1)).astype(np.float32))
         assert act == pytest.approx(per.mean(), abs=1e-7)
         st = nxt
+
+
+def test_oracle_seeded_weights_equal_the_packages(golden_lang):
+    """The CPU legs' seeded weights (oracle/lang.py) are the reference model's seed-0 stream."""
+    import hashlib
+    from oracle.lang import seeded_weights
+    w = seeded_weights()
+    assert hashlib.sha256(w.tobytes()).hexdigest() == str(golden_lang['bc250_weights_sha'])
+    small = LanguageConfig(columns=3, width=17, regions=2, ticks=3, idle_steps=1)
+    assert np.array_equal(seeded_weights(3, 17, 2, 7), init_packed_weights(small, seed=7))
