@@ -92,6 +92,13 @@ int ng_step_static(void *engine, int token, const float *state,
                    size_t state_count, float *next_state, float *logits,
                    float *hidden, float *activity);
 
+/* The input sigmoid 1/(1 + expf(-x)) and the feedback tanhf exactly as the
+ * tick kernels evaluate them on the device, for n inputs (host buffers;
+ * either output may be NULL).  They equal the host C library's values, which
+ * the reference CPU engine uses (NeuralEngine.cpp:9,84-85); this entry point
+ * exists to check that.  No reference counterpart. */
+int ng_math_eval(const float *x, size_t n, float *tanh_out, float *sigmoid_out);
+
 /* ------------------------------------------------------------------------ */
 /* Part 3: device-resident session pools (state stays in HBM between calls). */
 /* ------------------------------------------------------------------------ */

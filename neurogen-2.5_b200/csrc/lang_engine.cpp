@@ -4,6 +4,7 @@
 // weights resident in HBM, uploaded once at construction.
 #include "engine/NeuralEngine.h"
 #include "lang_engine.h"
+#include "math_tables.h"
 
 #include <algorithm>
 #include <cmath>
@@ -122,19 +123,26 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   tables.n_fb = d.n_fb;
   tables.n_out = d.n_out;
 
-  // Recurrent connectivity mask: same layer, a preferred feed-forward pair, or
-  // an inhibitory presynaptic cell within one layer; no autapses
-  // (src/native/NeuralEngine.cpp:41-56, neurogen/language/model.py:42-48).
-  static const int preferred[6][2] = {{4, 2}, {4, 3}, {2, 3}, {3, 5}, {5, 6}, {6, 4}};
-  std::vector<float> rec_gain(64 * 64, 0.f);
-  for (int post = 0; post < 64; ++post)
-    for (int pre = 0; pre < 64; ++pre) {
-      const int lp = col.layer()[pre], lq = col.layer()[post];
-      bool ok = lp == lq;
-      for (const auto &pr : preferred) ok = ok || (lp == pr[0] && lq == pr[1]);
-      ok = ok || (col.sign()[pre] < 0 && std::abs(lq - lp) <= 1);
-      rec_gain[post * 64 + pre] = (ok && post != pre) ? col.sign()[pre] : 0.f;
-    }
+  // Host-libm corrections of the tick kernels' sigmoid and tanh (built once
+  // per process, uploaded per model).
+  auto upload_table = [](const HostMathTable &h, DeviceBuffer &start, DeviceBuffer &entries) {
+    start.reset(h.start.size() * 4);
+    entries.reset(std::max<size_t>(h.entries.size(), 1) * 2);
+    NGB_CUDA(cudaMemcpy(start.as<void>(), h.start.data(), h.start.size() * 4, cudaMemcpyHostToDevice));
+    if (!h.entries.empty())
+      NGB_CUDA(cudaMemcpy(entries.as<void>(), h.entries.data(), h.entries.size() * 2, cudaMemcpyHostToDevice));
+    libm_match::MathTable t;
+    t.start = start.as<uint32_t>();
+    t.entries = entries.as<uint16_t>();
+    t.lo = h.lo;
+    t.hi = h.hi;
+    return t;
+  };
+  sig_tab = upload_table(sigmoid_table(), sig_start, sig_entries);
+  tanh_tab = upload_table(tanh_table(), tanh_start, tanh_entries);
+
+  // Recurrent connectivity gain [post][pre] (laminar rule, no autapses).
+  const std::vector<float> rec_gain = col.recurrent_gain();
 
   const float *p = data;
   auto take = [&](size_t count) {
@@ -286,6 +294,8 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       ta.spikes = sc.cnt + adv * d.R + r;
       ta.spikes_ld = long(A) * d.R;
       ta.tab = tables;
+      ta.sig_tab = sig_tab;
+      ta.tanh_tab = tanh_tab;
       ta.feat = sc.feat;
       if (!launch_ticks_cluster(ta, d.T, st)) {
         // No cluster shape for this column count: one launch per tick with a

@@ -77,6 +77,9 @@ public:
   std::string label;
   cudaStream_t stream = nullptr;
   UnitTables tables;
+  // Device copies of the host-libm correction tables (math_tables.h).
+  DeviceBuffer sig_start, sig_entries, tanh_start, tanh_entries;
+  libm_match::MathTable sig_tab, tanh_tab;
   DeviceBuffer emb, head_wp, head_b, head_wr;
   DeviceBuffer head_hi, head_lo; // tf32 split of head_wr for the tensor-core readout
   std::vector<RegionWeights> regions;

@@ -9,15 +9,11 @@
 //     -fmad=false and the inner loops use __fmul_rn/__fadd_rn explicitly);
 //   * expressions are evaluated in the same association order as the C++;
 //   * LayerNorm statistics are accumulated in fp64 (NeuralEngine.cpp:96-104);
-//   * exp is evaluated in fp64 and rounded once to fp32, which equals glibc's
-//     expf except in rare ties; tanh uses the identity
-//       tanh(x) = 1 - 2/(expm1(2x)+2)           for |x| >= 1,
-//       tanh(x) = -expm1(-2x)/(expm1(-2x)+2)     for |x| <  1,
-//     evaluated in fp32 around a once-rounded fp64 expm1, which is the form the
-//     host libm evaluates (it agrees with glibc 2.39 tanhf on ~98% of inputs,
-//     1 ulp otherwise).
-// The result is bit-identical to the reference library except where a libm
-// result differs by an ulp; the parity tests quantify that.
+//   * the input sigmoid and the feedback tanh return exactly the host C
+//     library's values (expf, tanhf): a formula evaluated identically on host
+//     and device, corrected by a table of the inputs where the library's
+//     result differs (libm_match.cuh, math_tables.cpp).
+// The result is bit-identical to the reference library.
 #include "lang_kernels.h"
 
 #include <cooperative_groups.h>
@@ -43,31 +39,6 @@ __device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ float host_expf(float x) { return (float)exp((double)x); }
-
-// 1 / (1 + exp(-x)) as NeuralEngine.cpp:9.
-__device__ __forceinline__ float host_sigmoid(float x) {
-  return __fdiv_rn(1.f, __fadd_rn(1.f, host_expf(-x)));
-}
-
-// tanh via the expm1 identity (see file header).
-__device__ __forceinline__ float host_tanh(float x) {
-  const float ax = fabsf(x);
-  float z;
-  if (ax >= 22.f) {
-    z = 1.f;
-  } else if (ax >= 1.f) {
-    const float t = (float)expm1((double)(2.f * ax));
-    z = __fsub_rn(1.f, __fdiv_rn(2.f, __fadd_rn(t, 2.f)));
-  } else if (ax < 0x1p-55f) {
-    z = ax;
-  } else {
-    const float t = (float)expm1((double)(-2.f * ax));
-    z = __fdiv_rn(-t, __fadd_rn(t, 2.f));
-  }
-  return x < 0.f ? -z : z;
 }
 
 // ---------------------------------------------------------------------------
@@ -717,8 +688,8 @@ __global__ void __launch_bounds__(64 * TK_SB) k_tick(TickArgs a) {
   // Input current (NeuralEngine.cpp:72-86).
   float current = exc ? .15f : .35f;
   const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
-  if (a.vin && ii >= 0) current = 3 * host_sigmoid(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii]);
-  if (fi >= 0) current = current + .5f * host_tanh(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi]);
+  if (a.vin && ii >= 0) current = 3 * libm_match::sigmoid_host(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii], a.sig_tab);
+  if (fi >= 0) current = current + .5f * libm_match::tanh_host(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi], a.tanh_tab);
 
   // Recurrent input, sequential in the presynaptic index (CPUBackend.cpp:28-30).
   float recurrent = 0.f;
@@ -809,8 +780,8 @@ __global__ void __launch_bounds__(64 * CPC) k_ticks_cluster(TickArgs a, int tick
       cnt[s] = st[4 * n + a.w + i];
       float cur = exc ? .15f : .35f;
       const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
-      if (a.vin && ii >= 0) cur = 3 * host_sigmoid(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii]);
-      if (fi >= 0) cur = cur + .5f * host_tanh(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi]);
+      if (a.vin && ii >= 0) cur = 3 * libm_match::sigmoid_host(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii], a.sig_tab);
+      if (fi >= 0) cur = cur + .5f * libm_match::tanh_host(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi], a.tanh_tab);
       current[s] = cur;
     }
   }

@@ -3,6 +3,8 @@
 // builds them.  All kernels reproduce the reference CPU engine's fp32
 // arithmetic operation by operation (see lang_kernels.cu).
 #pragma once
+#include "libm_match.cuh"
+
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -97,6 +99,9 @@ struct TickArgs {
   int *spikes;      // spike counter per session, stride spikes_ld
   long spikes_ld;
   UnitTables tab;
+  // Corrections that make the input sigmoid and feedback tanh equal the host
+  // C library's (libm_match.cuh).
+  libm_match::MathTable sig_tab, tanh_tab;
 };
 void launch_tick(const TickArgs &a, cudaStream_t s);
 // All `ticks` ticks of one region in one thread-block-cluster launch (trace

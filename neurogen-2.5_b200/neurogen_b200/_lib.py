@@ -29,7 +29,7 @@ EXPORTS = (
     'ng_net_synapses', 'ng_net_export', 'ng_net_set_state', 'ng_net_get_state', 'ng_net_run',
     'ng_net_run_device', 'ng_topology_create', 'ng_topology_destroy', 'ng_topology_synapses',
     'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static', 'ng_net_launch_kind',
-    'ng_net_create_partitioned', 'ng_nccl_unique_id',
+    'ng_net_create_partitioned', 'ng_nccl_unique_id', 'ng_math_eval',
 )
 
 
@@ -84,6 +84,8 @@ def library():
     lib.ng_advance.restype = ci
     lib.ng_step_static.argtypes = [vp, ci, F32, sz, F32, F32, F32, F32]
     lib.ng_step_static.restype = ci
+    lib.ng_math_eval.argtypes = [F32, sz, F32, F32]
+    lib.ng_math_eval.restype = ci
     lib.ng_state_size.argtypes = [vp]
     lib.ng_state_size.restype = sz
     lib.ng_parameter_count.argtypes = [ci, ci, ci]

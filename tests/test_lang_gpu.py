@@ -478,3 +478,42 @@ def test_readout_wait_runs_out_cleanly(tmp_path):
     assert out.returncode == 0, out.stderr[-3000:]
     assert 'raised: Readout kernel timed out' in out.stdout, out.stdout
     assert 'after: True' in out.stdout, out.stdout
+
+
+def libm_inputs():
+    """Every float of the binades where the host library and a correctly rounded evaluation
+    differ most ([2^-3, 2^-2), [2^-1, 1), [1, 2)), both signs, plus 4 M random floats of
+    magnitude 2^-30 .. 2^7 and the range edges."""
+    dense = np.concatenate([np.arange(np.float32(lo).view(np.uint32), np.float32(2 * lo).view(np.uint32),
+                                      dtype=np.uint32) for lo in (0.125, 0.5, 1.0)]).view(np.float32)
+    rng = np.random.default_rng(0)
+    rand = (rng.uniform(-30, 7, 4_000_000).astype(np.float32))
+    rand = (np.exp2(rand) * rng.choice([-1, 1], rand.size)).astype(np.float32)
+    edges = np.array([0.0, 2.0 ** -40, 2.0 ** -22, 16.75, 16.7501, 22.0, 21.999998, 88.8, 100.0, 1e30],
+                     np.float32)
+    x = np.concatenate([dense, -dense, rand, edges, -edges]).astype(np.float32)
+    return np.ascontiguousarray(x)
+
+
+def test_device_tanh_and_sigmoid_equal_the_host_library():
+    """The tick kernels' feedback tanh and input sigmoid return the host C library's tanhf and
+    1 / (1 + expf(-x)) bit for bit (the reference engine's functions; neither is correctly
+    rounded, so this needs the correction tables of libm_match.cuh)."""
+    import ctypes as ct
+    from neurogen_b200 import library
+    from oracle.lang import ORACLE_LIB
+    x = libm_inputs()
+    dt, ds = np.empty_like(x), np.empty_like(x)
+    lib = library()
+    assert lib.ng_math_eval(x, x.size, dt, ds) == 0, lib.ng_error().decode()
+    orc = ct.CDLL(str(ORACLE_LIB))
+    orc.om_libm_eval.argtypes = [ct.c_void_p, ct.c_size_t, ct.c_void_p, ct.c_void_p]
+    ht, hs = np.empty_like(x), np.empty_like(x)
+    orc.om_libm_eval(x.ctypes.data, x.size, ht.ctypes.data, hs.ctypes.data)
+    bad_t = int((dt.view(np.uint32) != ht.view(np.uint32)).sum())
+    bad_s = int((ds.view(np.uint32) != hs.view(np.uint32)).sum())
+    cr = np.tanh(x.astype(np.float64)).astype(np.float32)
+    not_cr = int((cr.view(np.uint32) != ht.view(np.uint32)).sum())
+    print(f'{x.size:,} inputs: tanh mismatches {bad_t}, sigmoid mismatches {bad_s} '
+          f'(host tanhf differs from correct rounding on {not_cr:,} of them)')
+    assert bad_t == 0 and bad_s == 0
