@@ -273,26 +273,51 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
     // 1. Membrane update of the held neurons.
     const int rs = (int)(t & dr_mask);
     const bool inflow = k < kRingSlots;
-    for (int i = tid; i < Pw * 32; i += RT) {
-      bool s = false;
-      if (i < Pc) {
-        int *slot = ring_s + rs * 2 * P + i;
-        int2 q = make_int2(slot[0], slot[P]);
+    // Two neurons a thread (P <= 2 * RT), computed side by side so their
+    // dependent chains interleave; the second is a duplicate of neuron 0,
+    // computed and discarded, where it does not exist.
+    {
+      const int i0 = tid, i1 = tid + RT;
+      const bool ok0 = i0 < Pc, ok1 = i1 < Pc;
+      const int j0 = ok0 ? i0 : 0, j1 = ok1 ? i1 : 0;
+      int2 q0 = make_int2(0, 0), q1 = make_int2(0, 0);
+      if (ok0) {
+        int *slot = ring_s + rs * 2 * P + j0;
+        q0 = make_int2(slot[0], slot[P]);
         slot[0] = 0;
         slot[P] = 0;
-        if (inflow) {
-          int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + i;
-          const int2 x = *g;
-          if (x.x | x.y) {
-            q.x += x.x;
-            q.y += x.y;
-            *g = make_int2(0, 0);
-          }
-        }
-        s = alif_math(d, t, gbase + i, q, v_s[i], a_s[i], ge_s[i], gi_s[i], ref_s[i]);
       }
-      const unsigned fired = __ballot_sync(0xffffffffu, s);
-      if (lane == 0) word_s[i >> 5] = fired;
+      if (ok1) {
+        int *slot = ring_s + rs * 2 * P + j1;
+        q1 = make_int2(slot[0], slot[P]);
+        slot[0] = 0;
+        slot[P] = 0;
+      }
+      if (inflow) {
+        if (ok0) {
+          int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + j0;
+          const int2 x = *g;
+          if (x.x | x.y) { q0.x += x.x; q0.y += x.y; *g = make_int2(0, 0); }
+        }
+        if (ok1) {
+          int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + j1;
+          const int2 x = *g;
+          if (x.x | x.y) { q1.x += x.x; q1.y += x.y; *g = make_int2(0, 0); }
+        }
+      }
+      float v0 = v_s[j0], a0 = a_s[j0], e0 = ge_s[j0], n0 = gi_s[j0];
+      float v1 = v_s[j1], a1 = a_s[j1], e1 = ge_s[j1], n1 = gi_s[j1];
+      int r0 = ref_s[j0], r1 = ref_s[j1];
+      const bool s0 = alif_math(d, t, gbase + j0, q0, v0, a0, e0, n0, r0) && ok0;
+      const bool s1 = alif_math(d, t, gbase + j1, q1, v1, a1, e1, n1, r1) && ok1;
+      if (ok0) { v_s[j0] = v0; a_s[j0] = a0; ge_s[j0] = e0; gi_s[j0] = n0; ref_s[j0] = r0; }
+      if (ok1) { v_s[j1] = v1; a_s[j1] = a1; ge_s[j1] = e1; gi_s[j1] = n1; ref_s[j1] = r1; }
+      const unsigned f0 = __ballot_sync(0xffffffffu, s0);
+      const unsigned f1 = __ballot_sync(0xffffffffu, s1);
+      if (lane == 0) {
+        if ((i0 >> 5) < Pw) word_s[i0 >> 5] = f0;
+        if ((i1 >> 5) < Pw) word_s[i1 >> 5] = f1;
+      }
     }
     __syncthreads();
     // 2. This CTA's spike ids into its reserved range of the tick's list.

@@ -1,6 +1,6 @@
 """Generate tests/golden/lang_golden.npz from the reference itself.
 
-Run in a container where the reference checkout is importable (default /root/reference) after
+Run in a container where the reference checkout is importable (its path as the first argument, or in NEUROGEN_REFERENCE) after
 `make -C oracle`.  It records, for fixed seeded inputs:
 
 * small config (columns 3, width 17, regions 2, ticks 3, idle 1) -- the configuration of the
@@ -16,6 +16,7 @@ Run in a container where the reference checkout is importable (default /root/ref
 Usage: python tests/golden/make_lang_golden.py [/path/to/reference]
 """
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -23,7 +24,7 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ['NEUROGEN_REFERENCE'])
 sys.path.insert(0, str(REFERENCE))
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / 'neurogen-2.5_b200'))

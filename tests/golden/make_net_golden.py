@@ -7,13 +7,14 @@ network engine's convention); the dynamics are equivariant under that permutatio
 
 Usage: python tests/golden/make_net_golden.py [/path/to/reference]
 """
+import os
 import sys
 from pathlib import Path
 
 import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
-REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ['NEUROGEN_REFERENCE'])
 sys.path.insert(0, str(REFERENCE))
 
 from neurogen.biology import BiologicalNetwork, BiologyConfig  # noqa: E402

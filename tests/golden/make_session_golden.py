@@ -1,15 +1,16 @@
 """Writes tests/golden/session_ref_small.pt: a ``neurogen-session-v2`` file saved by the reference
 runtime's own ``Session.save`` (neurogen/language/runtime.py:95-100) after one user turn, for a small
-seeded model.  Run where the reference checkout is importable (default /root/reference):
+seeded model.  Run where the reference checkout is importable (its path as the first argument, or in NEUROGEN_REFERENCE):
 
     python tests/golden/make_session_golden.py [/path/to/reference]
 """
+import os
 import sys
 from pathlib import Path
 
 import torch
 
-REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ['NEUROGEN_REFERENCE'])
 sys.path.insert(0, str(REFERENCE))
 
 from neurogen.language.config import LanguageConfig  # noqa: E402
