@@ -125,7 +125,7 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
 
   // Host-libm corrections of the tick kernels' sigmoid and tanh (built once
   // per process, uploaded per model).
-  auto upload_table = [](const HostMathTable &h, DeviceBuffer &start, DeviceBuffer &entries) {
+  auto upload_table = [](const HostMathTable &h, DeviceBuffer &start, DeviceBuffer &entries, DeviceBuffer &map, DeviceBuffer &skip) {
     start.reset(h.start.size() * 4);
     entries.reset(std::max<size_t>(h.entries.size(), 1) * 2);
     NGB_CUDA(cudaMemcpy(start.as<void>(), h.start.data(), h.start.size() * 4, cudaMemcpyHostToDevice));
@@ -136,10 +136,23 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
     t.entries = entries.as<uint16_t>();
     t.lo = h.lo;
     t.hi = h.hi;
+    t.shift = h.shift;
+    t.steps = h.steps;
+    skip.reset(h.skip.size() * 4);
+    NGB_CUDA(cudaMemcpy(skip.as<void>(), h.skip.data(), h.skip.size() * 4, cudaMemcpyHostToDevice));
+    t.skip = skip.as<float>();
+    if (!h.map.empty()) {
+      map.reset(h.map.size() * 4);
+      NGB_CUDA(cudaMemcpy(map.as<void>(), h.map.data(), h.map.size() * 4, cudaMemcpyHostToDevice));
+      t.map = map.as<uint32_t>();
+      t.map_lo = h.map_lo;
+      t.map_hi = h.map_hi;
+    }
     return t;
   };
-  sig_tab = upload_table(sigmoid_table(), sig_start, sig_entries);
-  tanh_tab = upload_table(tanh_table(), tanh_start, tanh_entries);
+  sig_tab = upload_table(sigmoid_table(false), sig_start, sig_entries, sig_map, sig_skip);
+  sig_neg_tab = upload_table(sigmoid_table(true), sig_neg_start, sig_neg_entries, sig_neg_map, sig_neg_skip);
+  tanh_tab = upload_table(tanh_table(), tanh_start, tanh_entries, tanh_map, tanh_skip);
 
   // Recurrent connectivity gain [post][pre] (laminar rule, no autapses).
   const std::vector<float> rec_gain = col.recurrent_gain();
@@ -295,6 +308,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       ta.spikes_ld = long(A) * d.R;
       ta.tab = tables;
       ta.sig_tab = sig_tab;
+      ta.sig_neg_tab = sig_neg_tab;
       ta.tanh_tab = tanh_tab;
       ta.feat = sc.feat;
       if (!launch_ticks_cluster(ta, d.T, st)) {

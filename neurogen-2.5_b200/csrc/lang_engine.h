@@ -78,8 +78,9 @@ public:
   cudaStream_t stream = nullptr;
   UnitTables tables;
   // Device copies of the host-libm correction tables (math_tables.h).
-  DeviceBuffer sig_start, sig_entries, tanh_start, tanh_entries;
-  libm_match::MathTable sig_tab, tanh_tab;
+  DeviceBuffer sig_start, sig_entries, sig_map, sig_skip, sig_neg_start, sig_neg_entries, sig_neg_map, sig_neg_skip,
+      tanh_start, tanh_entries, tanh_map, tanh_skip;
+  libm_match::MathTable sig_tab, sig_neg_tab, tanh_tab;
   DeviceBuffer emb, head_wp, head_b, head_wr;
   DeviceBuffer head_hi, head_lo; // tf32 split of head_wr for the tensor-core readout
   std::vector<RegionWeights> regions;

@@ -688,7 +688,7 @@ __global__ void __launch_bounds__(64 * TK_SB) k_tick(TickArgs a) {
   // Input current (NeuralEngine.cpp:72-86).
   float current = exc ? .15f : .35f;
   const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
-  if (a.vin && ii >= 0) current = 3 * libm_match::sigmoid_host(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii], a.sig_tab);
+  if (a.vin && ii >= 0) current = 3 * libm_match::sigmoid_host(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii], a.sig_tab, a.sig_neg_tab);
   if (fi >= 0) current = current + .5f * libm_match::tanh_host(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi], a.tanh_tab);
 
   // Recurrent input, sequential in the presynaptic index (CPUBackend.cpp:28-30).
@@ -767,10 +767,20 @@ __global__ void __launch_bounds__(64 * CPC) k_ticks_cluster(TickArgs a, int tick
   const bool exc = (a.tab.exc_mask >> id) & 1ull;
   const int n = a.n, i = col * 64 + id;
   float V[SB], trace[SB], adapt[SB], last[SB], cnt[SB], current[SB];
+  // Input current (NeuralEngine.cpp:72-86): a unit takes the input sigmoid
+  // (layer 4 E), the feedback tanh (layers 1, 5, 6) or neither; the library
+  // corrections of all SB sessions are looked up together.
+  const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
+  const bool sig = a.vin && ii >= 0, th = fi >= 0;
+  float x[SB], z[SB];
+  uint32_t key[SB];
+  int which[SB]; // table: 0 sigmoid (x >= 0), 1 sigmoid (x < 0), 2 tanh, -1 none
 #pragma unroll
   for (int s = 0; s < SB; ++s) {
     const int b = b0 + s;
-    V[s] = trace[s] = adapt[s] = last[s] = cnt[s] = current[s] = 0.f;
+    V[s] = trace[s] = adapt[s] = last[s] = cnt[s] = x[s] = 0.f;
+    which[s] = -1;
+    key[s] = 0u;
     if (b < a.B) {
       const float *st = a.state + (long)b * a.S + a.roff;
       V[s] = st[i];
@@ -778,12 +788,28 @@ __global__ void __launch_bounds__(64 * CPC) k_ticks_cluster(TickArgs a, int tick
       adapt[s] = st[2 * n + i];
       last[s] = st[3 * n + i];
       cnt[s] = st[4 * n + a.w + i];
-      float cur = exc ? .15f : .35f;
-      const int ii = a.tab.in_idx[id], fi = a.tab.fb_idx[id];
-      if (a.vin && ii >= 0) cur = 3 * libm_match::sigmoid_host(a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii], a.sig_tab);
-      if (fi >= 0) cur = cur + .5f * libm_match::tanh_host(a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi], a.tanh_tab);
-      current[s] = cur;
+      if (sig) x[s] = a.vin[(long)b * a.c * a.tab.n_in + col * a.tab.n_in + ii];
+      else if (th) x[s] = a.fb[(long)b * a.c * a.tab.n_fb + col * a.tab.n_fb + fi];
+      const uint32_t u = libm_match::bits_of(x[s]);
+      which[s] = sig ? (int)(u >> 31) : th ? 2 : -1;
+      key[s] = u & 0x7FFFFFFFu;
     }
+  }
+  // The formulas of all SB sessions side by side (independent FP64 chains).
+  double ed[SB];
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    ed[s] = 0.0;
+    z[s] = sig ? libm_match::sigmoid_formula_d(x[s], ed[s]) : th ? libm_match::tanh_formula_d(x[s], ed[s]) : 0.f;
+  }
+  int dl[SB];
+  libm_match::table_deltas<SB>(a.sig_tab, a.sig_neg_tab, a.tanh_tab, which, key, ed, dl);
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    float cur = exc ? .15f : .35f;
+    if (sig) cur = 3 * libm_match::add_ulps(z[s], dl[s]);
+    else if (th) cur = cur + .5f * libm_match::add_ulps(z[s], dl[s]);
+    current[s] = cur;
   }
   auto tr_at = [&](int buf, int ss, int cc) { return trb + ((buf * SB + ss) * CPC + cc) * 64; };
 #pragma unroll

@@ -101,7 +101,7 @@ struct TickArgs {
   UnitTables tab;
   // Corrections that make the input sigmoid and feedback tanh equal the host
   // C library's (libm_match.cuh).
-  libm_match::MathTable sig_tab, tanh_tab;
+  libm_match::MathTable sig_tab, sig_neg_tab, tanh_tab;
 };
 void launch_tick(const TickArgs &a, cudaStream_t s);
 // All `ticks` ticks of one region in one thread-block-cluster launch (trace

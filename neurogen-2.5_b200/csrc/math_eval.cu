@@ -12,14 +12,14 @@
 namespace ngb {
 namespace {
 __global__ void k_math_eval(const float *x, int n, float *tanh_out, float *sig_out, libm_match::MathTable tt,
-                            libm_match::MathTable st) {
+                            libm_match::MathTable sp, libm_match::MathTable sn) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (tanh_out) tanh_out[i] = libm_match::tanh_host(x[i], tt);
-  if (sig_out) sig_out[i] = libm_match::sigmoid_host(x[i], st);
+  if (sig_out) sig_out[i] = libm_match::sigmoid_host(x[i], sp, sn);
 }
 
-libm_match::MathTable upload(const HostMathTable &h, DeviceBuffer &start, DeviceBuffer &entries) {
+libm_match::MathTable upload(const HostMathTable &h, DeviceBuffer &start, DeviceBuffer &entries, DeviceBuffer &map, DeviceBuffer &skip) {
   start.reset(h.start.size() * 4);
   entries.reset((h.entries.size() + 1) * 2);
   NGB_CUDA(cudaMemcpy(start.as<void>(), h.start.data(), h.start.size() * 4, cudaMemcpyHostToDevice));
@@ -30,6 +30,18 @@ libm_match::MathTable upload(const HostMathTable &h, DeviceBuffer &start, Device
   t.entries = entries.as<uint16_t>();
   t.lo = h.lo;
   t.hi = h.hi;
+  t.shift = h.shift;
+  t.steps = h.steps;
+  skip.reset(h.skip.size() * 4);
+  NGB_CUDA(cudaMemcpy(skip.as<void>(), h.skip.data(), h.skip.size() * 4, cudaMemcpyHostToDevice));
+  t.skip = skip.as<float>();
+  if (!h.map.empty()) {
+    map.reset(h.map.size() * 4);
+    NGB_CUDA(cudaMemcpy(map.as<void>(), h.map.data(), h.map.size() * 4, cudaMemcpyHostToDevice));
+    t.map = map.as<uint32_t>();
+    t.map_lo = h.map_lo;
+    t.map_hi = h.map_hi;
+  }
   return t;
 }
 } // namespace
@@ -41,13 +53,15 @@ extern "C" int ng_math_eval(const float *x, size_t n, float *tanh_out, float *si
   return guarded([&] {
     if (!x || (!tanh_out && !sigmoid_out)) throw std::invalid_argument("Null input/output");
     require_sm100_device();
-    DeviceBuffer ts, te, ss, se, dx(n * 4 + 4), dt(n * 4 + 4), ds(n * 4 + 4);
-    const libm_match::MathTable tt = upload(tanh_table(), ts, te), st = upload(sigmoid_table(), ss, se);
+    DeviceBuffer ts, te, tm, tk, ps, pe, pm, pk, ns, ne, nm, nk, dx(n * 4 + 4), dt(n * 4 + 4), ds(n * 4 + 4);
+    const libm_match::MathTable tt = upload(tanh_table(), ts, te, tm, tk),
+                                sp = upload(sigmoid_table(false), ps, pe, pm, pk),
+                                sn = upload(sigmoid_table(true), ns, ne, nm, nk);
     NGB_CUDA(cudaMemcpy(dx.as<void>(), x, n * 4, cudaMemcpyHostToDevice));
     for (size_t o = 0; o < n; o += size_t(1) << 30) {
       const int m = int(std::min(n - o, size_t(1) << 30));
       k_math_eval<<<(m + 255) / 256, 256>>>(dx.as<float>() + o, m, tanh_out ? dt.as<float>() + o : nullptr,
-                                            sigmoid_out ? ds.as<float>() + o : nullptr, tt, st);
+                                            sigmoid_out ? ds.as<float>() + o : nullptr, tt, sp, sn);
       NGB_CUDA(cudaGetLastError());
     }
     if (tanh_out) NGB_CUDA(cudaMemcpy(tanh_out, dt.as<void>(), n * 4, cudaMemcpyDeviceToHost));

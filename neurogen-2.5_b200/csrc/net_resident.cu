@@ -15,7 +15,8 @@
 // a delivery is one add, one unsigned min and one shared-memory atomic.
 //
 // A tick is
-//   1. membrane update of the CTA's own neurons from its shared ring slot;
+//   1. membrane update of the CTA's own neurons from its shared ring slot
+//      (two neurons a thread when the CTA holds more neurons than threads);
 //   2. the CTA reserves a range of this tick's global spike list with one
 //      atomic (counters rotate over three ticks) and writes its spike ids;
 //   3. one grid barrier (bounded wait), after which the list is complete;
@@ -220,6 +221,25 @@ __device__ __forceinline__ bool grid_sync(const ResidentDev &r, unsigned target,
   return ok_s != 0;
 }
 
+// Read and clear a neuron's (E, I) arrivals in its shared ring slot.
+__device__ __forceinline__ int2 take_slot(int *slot, int P) {
+  const int2 q = make_int2(slot[0], slot[P]);
+  slot[0] = 0;
+  slot[P] = 0;
+  return q;
+}
+
+// Add a neuron's arrivals waiting in the global ring (the state of record
+// between launches) and clear them.
+__device__ __forceinline__ void take_global(int2 *g, int2 &q) {
+  const int2 x = *g;
+  if (x.x | x.y) {
+    q.x += x.x;
+    q.y += x.y;
+    *g = make_int2(0, 0);
+  }
+}
+
 __device__ __forceinline__ unsigned long long block_sum(unsigned long long v, unsigned long long *red_s) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -273,51 +293,56 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
     // 1. Membrane update of the held neurons.
     const int rs = (int)(t & dr_mask);
     const bool inflow = k < kRingSlots;
-    // Two neurons a thread (P <= 2 * RT), computed side by side so their
-    // dependent chains interleave; the second is a duplicate of neuron 0,
-    // computed and discarded, where it does not exist.
-    {
+    if (Pc > RT) {
+      // Two neurons a thread (P <= 2 * RT), computed side by side so their
+      // dependent chains interleave; where the second does not exist, a
+      // duplicate of neuron 0 is computed and discarded.
       const int i0 = tid, i1 = tid + RT;
       const bool ok0 = i0 < Pc, ok1 = i1 < Pc;
       const int j0 = ok0 ? i0 : 0, j1 = ok1 ? i1 : 0;
       int2 q0 = make_int2(0, 0), q1 = make_int2(0, 0);
-      if (ok0) {
-        int *slot = ring_s + rs * 2 * P + j0;
-        q0 = make_int2(slot[0], slot[P]);
-        slot[0] = 0;
-        slot[P] = 0;
-      }
-      if (ok1) {
-        int *slot = ring_s + rs * 2 * P + j1;
-        q1 = make_int2(slot[0], slot[P]);
-        slot[0] = 0;
-        slot[P] = 0;
-      }
+      if (ok0) q0 = take_slot(ring_s + rs * 2 * P + j0, P);
+      if (ok1) q1 = take_slot(ring_s + rs * 2 * P + j1, P);
       if (inflow) {
-        if (ok0) {
-          int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + j0;
-          const int2 x = *g;
-          if (x.x | x.y) { q0.x += x.x; q0.y += x.y; *g = make_int2(0, 0); }
-        }
-        if (ok1) {
-          int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + j1;
-          const int2 x = *g;
-          if (x.x | x.y) { q1.x += x.x; q1.y += x.y; *g = make_int2(0, 0); }
-        }
+        int2 *g = d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase;
+        if (ok0) take_global(g + j0, q0);
+        if (ok1) take_global(g + j1, q1);
       }
       float v0 = v_s[j0], a0 = a_s[j0], e0 = ge_s[j0], n0 = gi_s[j0];
       float v1 = v_s[j1], a1 = a_s[j1], e1 = ge_s[j1], n1 = gi_s[j1];
       int r0 = ref_s[j0], r1 = ref_s[j1];
       const bool s0 = alif_math(d, t, gbase + j0, q0, v0, a0, e0, n0, r0) && ok0;
       const bool s1 = alif_math(d, t, gbase + j1, q1, v1, a1, e1, n1, r1) && ok1;
-      if (ok0) { v_s[j0] = v0; a_s[j0] = a0; ge_s[j0] = e0; gi_s[j0] = n0; ref_s[j0] = r0; }
-      if (ok1) { v_s[j1] = v1; a_s[j1] = a1; ge_s[j1] = e1; gi_s[j1] = n1; ref_s[j1] = r1; }
+      if (ok0) {
+        v_s[j0] = v0;
+        a_s[j0] = a0;
+        ge_s[j0] = e0;
+        gi_s[j0] = n0;
+        ref_s[j0] = r0;
+      }
+      if (ok1) {
+        v_s[j1] = v1;
+        a_s[j1] = a1;
+        ge_s[j1] = e1;
+        gi_s[j1] = n1;
+        ref_s[j1] = r1;
+      }
       const unsigned f0 = __ballot_sync(0xffffffffu, s0);
       const unsigned f1 = __ballot_sync(0xffffffffu, s1);
       if (lane == 0) {
         if ((i0 >> 5) < Pw) word_s[i0 >> 5] = f0;
         if ((i1 >> 5) < Pw) word_s[i1 >> 5] = f1;
       }
+    } else {
+      // One neuron a thread (small networks).
+      bool s0 = false;
+      if (tid < Pc) {
+        int2 q = take_slot(ring_s + rs * 2 * P + tid, P);
+        if (inflow) take_global(d.ring + (size_t)(t & (kRingSlots - 1)) * d.n + gbase + tid, q);
+        s0 = alif_math(d, t, gbase + tid, q, v_s[tid], a_s[tid], ge_s[tid], gi_s[tid], ref_s[tid]);
+      }
+      const unsigned f0 = __ballot_sync(0xffffffffu, s0);
+      if (lane == 0 && (tid >> 5) < Pw) word_s[tid >> 5] = f0;
     }
     __syncthreads();
     // 2. This CTA's spike ids into its reserved range of the tick's list.
