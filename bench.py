@@ -284,7 +284,8 @@ def tick_traffic(workload, mode, rate):
 
 
 KERNEL_OF_LAUNCH = {'fused': 'k_net_fused', 'split': 'tick = k_net_alif + k_net_push',
-                    'resident': 'k_net_resident (persistent, 2,048 ticks a launch)'}
+                    'resident': 'k_net_resident (persistent, serial tick, 2,048 ticks a launch)',
+                    'resident-pipelined': 'k_net_pipe (persistent, pipelined tick, 2,048 ticks a launch)'}
 
 
 def tick_launches(mode, ticks):
@@ -325,6 +326,7 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
         synapses = net.synapses
     setup_s = time.time() - t0
     mode = net.launch
+    shape = 'resident-pipelined' if net.resident_tick == 'pipelined' else mode
     stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
@@ -358,14 +360,14 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
         'higher_is_better': True, 'scaling': 'strong' if part else 'weak', 'vs_baseline': None,
         'dtype': 'fp32', 'data': 'synthetic', 'config': tick_config_dict(name, oc, dist.world, ticks),
         'measured': {'spike_rate': spikes / total_ticks / cfg.n, 'events_per_tick': events / total_ticks,
-                     'launch': mode, 'setup_s': round(setup_s, 2)},
+                     'launch': mode, 'resident_tick': net.resident_tick, 'setup_s': round(setup_s, 2)},
         'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
                      'frac': achieved / peak_total,
-                     'traffic': (tick_traffic(WORKLOAD_NAMES[name], mode, spikes / total_ticks / cfg.n)
+                     'traffic': (tick_traffic(WORKLOAD_NAMES[name], shape, spikes / total_ticks / cfg.n)
                                  if not part else None),
                      'traffic_unit': 'bytes/tick (ncu, scaled by spike rate)', 'bytes_per_tick': b_tick,
-                     'kernel': KERNEL_OF_LAUNCH[mode], 'peak_source': src},
+                     'kernel': KERNEL_OF_LAUNCH[shape], 'peak_source': src},
         'gpu_launches': tick_launches(mode, ticks) * steps,
         'clocks': clk.summary(),
     }

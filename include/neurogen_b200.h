@@ -231,8 +231,8 @@ void *ng_net_create_topology(const void *topology);
  * rank's synapses, with global neuron indices. */
 int64_t ng_net_synapses(void *net);
 
-/* Launch shape the network runs with: 1 fused, 2 split, 3 resident; -1 on a
- * null handle.  No counterpart in the reference (its isolated-tick network is
+/* Launch shape the network runs with: 1 fused, 2 split, 3 resident with the
+ * serial tick, 4 resident with the pipelined tick; -1 on a null handle.  No counterpart in the reference (its isolated-tick network is
  * biology.py's NumPy loop). */
 int ng_net_launch_kind(void *net);
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay,

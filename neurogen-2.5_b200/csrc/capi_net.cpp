@@ -129,7 +129,8 @@ int64_t ng_net_synapses(void *net) { return net ? static_cast<Network *>(net)->s
 int ng_net_launch_kind(void *net) {
   if (!net) return -1;
   const Network &w = *static_cast<Network *>(net);
-  return w.resident() ? 3 : w.split() ? 2 : 1;
+  if (w.resident()) return w.resident_plan().pipe ? 4 : 3;
+  return w.split() ? 2 : 1;
 }
 
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay, float *weight) {

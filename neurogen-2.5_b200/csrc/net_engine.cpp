@@ -803,6 +803,15 @@ bool Network::plan_resident(int max_delay, bool required) {
   r.ctas = (n_ + P - 1) / P;
   r.ring_depth = dr;
   r.ev64 = ev64 ? 1 : 0;
+  // Tick of the resident launch: NEUROGEN_RESIDENT_MODE=pipe | serial (the
+  // default below), NEUROGEN_RESIDENT_MEMBER_WARPS=8 | 16 the pipelined tick's
+  // membrane group.  The pipelined push addresses a CTA's rows by 32-bit
+  // offsets from its first row.
+  r.pipe = kResidentPipeDefault;
+  if (const char *env = std::getenv("NEUROGEN_RESIDENT_MODE")) r.pipe = std::string(env) == "pipe" ? 1 : 0;
+  if (!dev_.bsr && nnz_ + int64_t(kRowPad) * n_pre_ >= (int64_t(1) << 32)) r.pipe = 0;
+  r.member_warps = 16;
+  if (const char *env = std::getenv("NEUROGEN_RESIDENT_MEMBER_WARPS")) r.member_warps = std::atoi(env) == 8 ? 8 : 16;
   // Failure-path tests: an unreachable first barrier, so every CTA's bounded
   // wait runs out and the launch reports the error instead of running.
   if (const char *env = std::getenv("NEUROGEN_TEST_RESIDENT_STALL")) r.stall_test = std::atoi(env) ? 1 : 0;
@@ -811,7 +820,7 @@ bool Network::plan_resident(int max_delay, bool required) {
   if (smem + 2048 > size_t(optin)) // static shared memory and slack
     return fail(std::to_string(P) + " neurons a CTA with a " + std::to_string(dr) +
                 "-slot ring need more shared memory than a CTA has");
-  if (resident_max_ctas(ev64, smem) < r.ctas)
+  if (resident_max_ctas(r, dev_.bsr != 0, smem) < r.ctas)
     return fail("the device cannot hold " + std::to_string(r.ctas) + " resident CTAs at once");
   res_ = r;
   return true;
@@ -822,7 +831,7 @@ bool Network::plan_resident(int max_delay, bool required) {
 void Network::build_owner_blocks() {
   ResidentDev &r = res_;
   const size_t C = size_t(r.ctas);
-  res_lists_.reset(2 * size_t(n_pre_) * 4);
+  res_lists_.reset(3 * size_t(n_pre_) * 4);
   res_sync_.reset(16);
   res_err_.reset(4);
   NGB_CUDA(cudaMemset(res_sync_.as<void>(), 0, 16));

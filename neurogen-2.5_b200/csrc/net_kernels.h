@@ -78,21 +78,28 @@ void launch_add_tick(long long *t_dev, long long delta, cudaStream_t s);
 // state and a ring of ring_depth slots in shared memory.
 constexpr int kResidentThreads = 1024;
 constexpr int kOwnerBlockSlots = 8; // event words per owner block
+constexpr int kResidentPipeDefault = 0; // resident tick by default: 0 serial, 1 pipelined
 struct ResidentDev {
   int ctas;           // C (all co-resident)
   int per_cta;        // P, a multiple of 32, at most 2048
   int ring_depth;     // Dr: power of two >= the largest delay; 2*(Dr+1)*P < 2^16
   int ev64;           // 1: 64-bit events (fp32 weights), 0: 32-bit (fp16)
   int stall_test;     // failure-path tests only: 1 makes the first barrier wait run out
+  // 0: serial tick (membrane, list, barrier, delivery of every synapse in turn);
+  // 1: pipelined tick (delay-1 synapses pushed into the global ring by the
+  //    spiking neuron's CTA; owner blocks hold delay>=2 synapses only and are
+  //    delivered by a warp group while the membrane warps run the next tick).
+  int pipe;
+  int member_warps;   // pipelined: warps of the membrane group (8 or 16)
   const void *blocks; // [n_pre][C] owner blocks of 8 events, then overflow blocks
-  int *lists;         // [2][n_pre] spike ids of the tick, by tick parity
+  int *lists;         // [3][n_pre] spike ids of the tick (serial: by parity; pipelined: by t%3)
   unsigned *sync;     // [0] grid barrier counter, [1 + t%3] list length of tick t;
                       // zeroed before each launch
   int *err;           // set to 1 by a barrier timeout
 };
 size_t resident_smem_bytes(const ResidentDev &r);
-// Co-resident CTAs of the resident kernel at this shared-memory size (0: none).
-int resident_max_ctas(bool ev64, size_t smem);
+// Co-resident CTAs of the plan's kernel at this shared-memory size (0: none).
+int resident_max_ctas(const ResidentDev &r, bool bsr, size_t smem);
 // ticks ticks from tick t0; spikes_out [ticks][words] and counts [ticks][2] optional.
 cudaError_t launch_net_resident(const NetDev &d, const ResidentDev &r, long long t0, int ticks, uint32_t *spikes_out,
                                 unsigned long long *counts, int words, cudaStream_t s);

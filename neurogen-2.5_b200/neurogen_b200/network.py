@@ -130,7 +130,12 @@ class Network:
     @property
     def launch(self):
         """Launch shape in use: 'fused', 'split' or 'resident'."""
-        return {1: 'fused', 2: 'split', 3: 'resident'}[self.lib.ng_net_launch_kind(self.h)]
+        return {1: 'fused', 2: 'split', 3: 'resident', 4: 'resident'}[self.lib.ng_net_launch_kind(self.h)]
+
+    @property
+    def resident_tick(self):
+        """The resident launch's tick: 'pipelined' or 'serial' (None for the other launch shapes)."""
+        return {3: 'serial', 4: 'pipelined'}.get(self.lib.ng_net_launch_kind(self.h))
 
     def export(self):
         m = self.synapses

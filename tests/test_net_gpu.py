@@ -15,8 +15,22 @@ from oracle.net import NetOracle, unpack_spikes
 
 pytestmark = pytest.mark.gpu
 
-LAUNCH = {'fused': 1, 'split': 2, 'resident': 3}
+# 'resident' is the resident launch with its default tick; 'resident_pipe' and 'resident_serial'
+# select the pipelined and the serial tick explicitly.
+LAUNCH = {'fused': 1, 'split': 2, 'resident': 3, 'resident_pipe': 3, 'resident_serial': 3}
 LAUNCHES = list(LAUNCH)
+
+
+@pytest.fixture(autouse=True)
+def resident_mode(request, monkeypatch):
+    """Selects the resident tick (read at network creation) for tests parametrized by launch
+    shape ('resident_pipe', 'resident_serial') or by mode ('pipe', 'serial')."""
+    params = getattr(getattr(request.node, 'callspec', None), 'params', {})
+    mode = {'resident_pipe': 'pipe', 'resident_serial': 'serial'}.get(params.get('launch'), params.get('mode'))
+    if mode:
+        monkeypatch.setenv('NEUROGEN_RESIDENT_MODE', mode)
+    else:
+        monkeypatch.delenv('NEUROGEN_RESIDENT_MODE', raising=False)
 
 
 def run_both(cfg, ticks, state=None):
@@ -50,12 +64,12 @@ def test_isolated_8k_bit_exact_200_ticks(launch):
     assert_same_state(net, orc)
 
 
-@pytest.mark.parametrize('storage,launch', [('csr', 'fused'), ('csr', 'split'), ('csr', 'resident'),
-                                            ('bsr', 'fused'), ('bsr', 'split'), ('bsr', 'resident')])
+@pytest.mark.parametrize('storage', ['csr', 'bsr'])
+@pytest.mark.parametrize('launch', LAUNCHES)
 def test_block_matrix_both_storages_bit_exact(storage, launch):
     cfg = default_config(n=4096, n_exc=3277, topology='bsr16', bsr_blocks=32, bsr_fill=64,
                          weight_kind='halfnormal_f16', w_mu=0.0, w_sigma=0.05, storage=storage,
-                         drive_kind='imposed', drive_p=0.03, seed=4, launch=launch)
+                         drive_kind='imposed', drive_p=0.03, seed=4, launch=LAUNCH[launch])
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 60)
     np.testing.assert_array_equal(gs, os_)
     np.testing.assert_array_equal(gc, oc)
@@ -65,7 +79,8 @@ def test_block_matrix_both_storages_bit_exact(storage, launch):
 @pytest.mark.parametrize('launch', LAUNCHES)
 def test_fixed_fanin_fp16_imposed_bit_exact(launch):
     cfg = default_config(n=16384, n_exc=13107, topology='fixed_fanin', fanin=128, weight_kind='halfnormal_f16',
-                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8, launch=launch)
+                         w_mu=0.0, w_sigma=0.05, drive_kind='imposed', drive_p=0.05, seed=8,
+                         launch=LAUNCH[launch])
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 40)
     np.testing.assert_array_equal(gs, os_)
     np.testing.assert_array_equal(gc, oc)
@@ -75,11 +90,12 @@ def test_fixed_fanin_fp16_imposed_bit_exact(launch):
 @pytest.mark.parametrize('launch', LAUNCHES)
 def test_ragged_sizes_and_empty_network(launch):
     # n not a multiple of 32 (partial last warp) and an empty synapse set.
-    cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3, launch=launch)
+    cfg = default_config(n=1000, n_exc=777, p_connect=0.05, drive_ns=16.0, drive_p=0.05, seed=3,
+                         launch=LAUNCH[launch])
     net, orc, (gs, gc), (os_, oc) = run_both(cfg, 50)
     np.testing.assert_array_equal(gs, os_)
     assert_same_state(net, orc)
-    cfg0 = default_config(n=37, n_exc=30, p_connect=0.0, drive_ns=30.0, drive_p=0.2, seed=1, launch=launch)
+    cfg0 = default_config(n=37, n_exc=30, p_connect=0.0, drive_ns=30.0, drive_p=0.2, seed=1, launch=LAUNCH[launch])
     net, orc, (gs, gc), (os_, oc) = run_both(cfg0, 20)
     assert Topology(cfg0).synapses == 0
     np.testing.assert_array_equal(gs, os_)
@@ -197,8 +213,9 @@ def test_pipelined_graph_full_size():
     assert b.stats() == (int(ca[:, 0].sum()), int(ca[:, 1].sum()))
 
 
+@pytest.mark.parametrize('mode', ['pipe', 'serial'])
 @pytest.mark.parametrize('storage', ['csr', 'bsr'])
-def test_resident_full_size_equals_split(storage):
+def test_resident_full_size_equals_split(storage, mode):
     """N=262,144 at 5%, fixed fan-in CSR or 16x16 blocks: the resident launch (state and ring in
     shared memory, owner blocks with overflow chains, built from either storage) gives every spike,
     count and state bit of the split launch, across launch boundaries (2,048 ticks a launch) and a
@@ -280,7 +297,8 @@ print('after:', int(c[:, 0].sum()))
 '''
 
 
-def test_resident_barrier_wait_runs_out_cleanly(tmp_path):
+@pytest.mark.parametrize('mode', ['pipe', 'serial'])
+def test_resident_barrier_wait_runs_out_cleanly(tmp_path, mode):
     """The grid barrier's wait is bounded: with an unreachable target every CTA gives up after its
     limit, the host raises, and the same process creates and runs a new network afterwards."""
     import subprocess

@@ -62,8 +62,11 @@ def assert_state_close(cfg, got, want, where=''):
 # ---------------------------------------------------------------------------
 # Scaled tick, N=262,144 (resident launch), 100 ticks against the oracle.
 # ---------------------------------------------------------------------------
+@pytest.mark.parametrize('mode', ['pipe', 'serial'])
 @pytest.mark.parametrize('storage', ['csr', 'bsr'])
-def test_scaled_262k_resident_100_ticks_vs_oracle(storage):
+def test_scaled_262k_resident_100_ticks_vs_oracle(storage, mode, monkeypatch):
+    # mode: the pipelined or the serial resident tick.
+    monkeypatch.setenv('NEUROGEN_RESIDENT_MODE', mode)
     cfg = scaled_262k(storage, rate=0.03)
     topo = Topology(cfg)
     net = topo.network()
