@@ -119,6 +119,10 @@ class NetOracle:
         lib.on_set_state.argtypes = [ct.c_void_p] + [ct.c_void_p] * 6 + [ct.c_int64]
         lib.on_get_state.argtypes = [ct.c_void_p] + [ct.c_void_p] * 7
         lib.on_set_state64.argtypes = [ct.c_void_p] + [ct.c_void_p] * 5
+        lib.on_set_plasticity.argtypes = [ct.c_void_p, ct.POINTER(Plastic)]
+        lib.on_learn_probe.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_int]
+        lib.on_get_plasticity.argtypes = [ct.c_void_p] + [ct.c_void_p] * 7
+        lib.on_get_plasticity64.argtypes = [ct.c_void_p] + [ct.c_void_p] * 7
         self.params = params_from(cfg)
         self.n = self.params.n
         self.words = (self.n + 31) // 32
@@ -126,6 +130,8 @@ class NetOracle:
                       ((pre, np.int32), (post, np.int32), (delay, np.int32), (weight, np.float32),
                        (weight if weight64 is None else weight64, np.float64))]
         self.h = lib.on_create_w(ct.byref(self.params), len(self._keep[0]), *[_p(x) for x in self._keep])
+        # Contacts are stored by presynaptic cell, stable in input order.
+        self.order = np.argsort(self._keep[0], kind='stable')
 
     def __del__(self):
         if getattr(self, 'h', None):
@@ -172,6 +178,43 @@ class NetOracle:
         tick = np.zeros(1, np.int64)
         self.lib.on_get_state(self.h, _p(v), _p(a), _p(ge), _p(gi), _p(ref), _p(ring), _p(tick))
         return dict(v=v, a=a, ge=ge, gi=gi, ref=ref, ring=ring, tick=int(tick[0]))
+
+
+    # ---- plasticity (oracle/net_oracle.c: biology.py:182-218 learn) ----
+    def set_plasticity(self, on=True, stdp_rate=.005, inhibitory_rate=.002, target_hz=5.0, scaling_tau_ms=1e5):
+        """Learning every tick from now on (traces start at zero); on=False keeps the weights and
+        still updates the traces, as biology.py does with plasticity off."""
+        self.lib.on_set_plasticity(self.h, ct.byref(Plastic(int(on), stdp_rate, inhibitory_rate, target_hz,
+                                                            scaling_tau_ms)))
+
+    def learn_probe(self, arrivals, spikes, fp64=False):
+        """One learn() step with given arrival flags (per contact, input order) and spikes (per
+        cell), the reference's probe of its rule."""
+        arr = np.zeros(len(self.order), np.uint8)
+        arr[:] = np.asarray(arrivals, bool)[self.order]
+        spk = np.ascontiguousarray(spikes, np.uint8)
+        self.lib.on_learn_probe(self.h, _p(arr), _p(spk), int(fp64))
+
+    def plasticity_state(self, fp64=False):
+        """Weights and traces per contact in input order, post trace and rate per cell."""
+        m, n = len(self.order), self.n
+        dt = np.float64 if fp64 else np.float32
+        per_edge = [np.zeros(m, dt) for _ in range(5)]
+        post_tr, rate = np.zeros(n, dt), np.zeros(n, dt)
+        fn = self.lib.on_get_plasticity64 if fp64 else self.lib.on_get_plasticity
+        fn(self.h, *[_p(x) for x in per_edge], _p(post_tr), _p(rate))
+        out = {}
+        for k, x in zip(('weight', 'pre_trace', 'potential_trace', 'coactivity', 'usage'), per_edge):
+            y = np.empty_like(x)
+            y[self.order] = x
+            out[k] = y
+        out.update(post_trace=post_tr, rate=rate)
+        return out
+
+
+class Plastic(ct.Structure):
+    _fields_ = [('on', ct.c_int32), ('stdp_rate', ct.c_float), ('inh_rate', ct.c_float),
+                ('target_hz', ct.c_float), ('scaling_tau_ms', ct.c_float)]
 
 
 def unpack_spikes(words, n):

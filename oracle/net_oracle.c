@@ -12,8 +12,14 @@
  *       spike at V >= -50 mV -> reset -65 mV, adaptation += 15 pA (E) (:161-166)
  *     - emissions scheduled into slot (t + d) after all cells advanced (:174-176)
  *   E/I split of arrivals by presynaptic sign as include/engine/SparseKernels.cuh:229-287.
- * Plasticity, rewiring and Poisson background (biology.py:151,171-173) are out
- * of scope; an optional Bernoulli drive replaces the background.
+ * Optional plasticity (on_set_plasticity): biology.py:182-218 BiologicalNetwork.learn
+ * -- pair STDP with soft bounds on E contacts, Vogels-style inhibitory rule on
+ * I->E contacts, multiplicative synaptic scaling toward the target rate, weight
+ * clipping, and the pre/post/potential traces, coactivity and usage -- plus the
+ * rate trace of step() (:167-168); learning runs after the membrane update and
+ * before the tick's emissions, which carry the new weights (:169-176).
+ * Rewiring and Poisson background (biology.py:151,171-173,220-) are out of
+ * scope; an optional Bernoulli drive replaces the background.
  *
  * Two modes:
  *   fp32 -- the exact arithmetic contract of the CUDA engine: fp32 state, the
@@ -56,6 +62,13 @@ typedef struct {
   double *v64, *a64, *ge64, *gi64, *ref64;
   double *ring64; /* [RING][n][2] */
   int64_t tick;
+  /* plasticity (on_set_plasticity); per-synapse arrays in the stored order */
+  int32_t plastic;
+  float stdp_rate, inh_rate, target_hz, scaling_tau_ms;
+  float *pre_tr, *pot_tr, *coact, *usage, *post_tr, *rate;            /* fp32 */
+  double *pre_tr64, *pot_tr64, *coact64, *usage64, *post_tr64, *rate64; /* fp64 */
+  uint8_t *hist;   /* [RING][n] spikes of the last RING ticks (fp32 mode) */
+  uint8_t *hist64; /* the same for the fp64 mode */
 } on_net;
 
 /* splitmix64 finaliser (S. Vigna, public domain) used as a counter-based RNG. */
@@ -107,6 +120,9 @@ void on_destroy(void *h) {
   free(o->row); free(o->post); free(o->delay); free(o->w); free(o->w64);
   free(o->v); free(o->a); free(o->ge); free(o->gi); free(o->ref); free(o->ring);
   free(o->v64); free(o->a64); free(o->ge64); free(o->gi64); free(o->ref64); free(o->ring64);
+  free(o->pre_tr); free(o->pot_tr); free(o->coact); free(o->usage); free(o->post_tr); free(o->rate);
+  free(o->pre_tr64); free(o->pot_tr64); free(o->coact64); free(o->usage64); free(o->post_tr64);
+  free(o->rate64); free(o->hist); free(o->hist64);
   free(o);
 }
 
@@ -188,6 +204,188 @@ void on_get_state(void *h, float *v, float *a, float *ge, float *gi, int32_t *re
   if (tick) *tick = o->tick;
 }
 
+
+/* ---- plasticity: biology.py:182-218 (learn) and :167-168 (rate) ---- */
+
+typedef struct {
+  int32_t on;
+  float stdp_rate, inh_rate, target_hz, scaling_tau_ms; /* .005, .002, 5, 100000 */
+} on_plastic;
+
+/* Switches learning on (traces start at zero) or off. */
+void on_set_plasticity(void *h, const on_plastic *pl) {
+  on_net *o = (on_net *)h;
+  const size_t E = (size_t)(o->nnz ? o->nnz : 1), N = (size_t)o->p.n;
+  o->plastic = pl->on;
+  o->stdp_rate = pl->stdp_rate; o->inh_rate = pl->inh_rate;
+  o->target_hz = pl->target_hz; o->scaling_tau_ms = pl->scaling_tau_ms;
+  if (!o->pre_tr) {
+    o->pre_tr = calloc(E, 4); o->pot_tr = calloc(E, 4); o->coact = calloc(E, 4); o->usage = calloc(E, 4);
+    o->post_tr = calloc(N, 4); o->rate = calloc(N, 4);
+    o->pre_tr64 = calloc(E, 8); o->pot_tr64 = calloc(E, 8); o->coact64 = calloc(E, 8);
+    o->usage64 = calloc(E, 8); o->post_tr64 = calloc(N, 8); o->rate64 = calloc(N, 8);
+    o->hist = calloc(RING * N, 1); o->hist64 = calloc(RING * N, 1);
+  }
+}
+
+/* Constants of the fp32 contract: the reference's expressions in double,
+ * rounded once to float. */
+typedef struct {
+  float decay, slow, one_minus_slow, rate_inc, per_ms, alpha, dt;
+} on_lc;
+
+static on_lc lc_of(const on_net *o) {
+  const double dt = o->p.dt;
+  on_lc c;
+  c.decay = (float)exp(-dt / 20.0);
+  c.slow = (float)exp(-dt / 1000.0);
+  c.one_minus_slow = (float)(1.0 - exp(-dt / 1000.0));
+  c.rate_inc = (float)((1.0 - exp(-dt / 1000.0)) * 1000.0 / dt);
+  c.per_ms = (float)(1000.0 / dt);
+  c.alpha = (float)(2.0 * (double)o->target_hz * .020);
+  c.dt = (float)dt;
+  return c;
+}
+
+/* One learning step in the fp32 contract, every operation rounded as written.
+ * arr(e): the contact's presynaptic spike d ticks ago arrives now (biology.py:
+ * arrivals = queued amplitude > 0, and potential arrivals: the same for every
+ * stored contact); spk(i): this tick's spikes.  The weight's magnitude learns;
+ * its sign stays the presynaptic cell's. */
+static void learn32(on_net *o, const uint8_t *arr, const uint8_t *spk) {
+  const on_params *p = &o->p;
+  const on_lc c = lc_of(o);
+  const float stdp = o->stdp_rate, inh = o->inh_rate, tgt = o->target_hz, tau_s = o->scaling_tau_ms;
+  for (int32_t i = 0; i < p->n; ++i) {
+    for (int64_t e = o->row[i]; e < o->row[i + 1]; ++e) {
+      const float w0 = o->w[e];
+      if (w0 == 0.f) continue; /* not a contact */
+      const int32_t q = o->post[e];
+      const float a = arr[e] ? 1.f : 0.f, post = spk[q] ? 1.f : 0.f;
+      const float pt = o->pre_tr[e] * c.decay, pot = o->pot_tr[e] * c.decay, pq = o->post_tr[q] * c.decay;
+      float w = fabsf(w0);
+      const int exc = i < p->n_exc;
+      if (o->plastic) {
+        float delta;
+        if (exc) {
+          delta = stdp * ((pt * post) * (4.f - w) - ((1.05f * pq) * a) * w);
+        } else {
+          delta = inh * (a * (pq - c.alpha) + pt * post);
+          delta = delta * (q < p->n_exc ? 1.f : 0.f);
+        }
+        w = w + delta;
+        if (exc) {
+          float x = (((tgt - o->rate[q]) / tgt) * c.dt) / tau_s;
+          x = x < -.001f ? -.001f : (x > .001f ? .001f : x);
+          w = w * ng_expf(x);
+        }
+        const float hi = exc ? 4.f : 12.f;
+        w = w < .01f ? .01f : w;
+        w = w > hi ? hi : w;
+      }
+      o->coact[e] = o->coact[e] * c.slow + (c.one_minus_slow * pot) * post;
+      o->usage[e] = o->usage[e] * c.slow + ((c.one_minus_slow * a) * c.per_ms);
+      o->pre_tr[e] = pt + a;
+      o->pot_tr[e] = pot + a;
+      o->w[e] = w0 < 0.f ? -w : w;
+    }
+  }
+  for (int32_t i = 0; i < p->n; ++i) o->post_tr[i] = o->post_tr[i] * c.decay + (spk[i] ? 1.f : 0.f);
+}
+
+/* The same step in double, in biology.py's operation order (fp64 mode). */
+static void learn64(on_net *o, const uint8_t *arr, const uint8_t *spk) {
+  const on_params *p = &o->p;
+  const double dt = p->dt, decay = exp(-dt / 20.0), slow = exp(-dt / 1000.0);
+  const double stdp = o->stdp_rate, inh = o->inh_rate, tgt = o->target_hz, tau_s = o->scaling_tau_ms;
+  const double alpha = 2.0 * tgt * .020;
+  for (int32_t i = 0; i < p->n; ++i) {
+    for (int64_t e = o->row[i]; e < o->row[i + 1]; ++e) {
+      const double w0 = o->w64[e];
+      if (w0 == 0.0) continue;
+      const int32_t q = o->post[e];
+      const double a = arr[e] ? 1.0 : 0.0, post = spk[q] ? 1.0 : 0.0;
+      const double pt = o->pre_tr64[e] * decay, pot = o->pot_tr64[e] * decay, pq = o->post_tr64[q] * decay;
+      double w = fabs(w0);
+      const int exc = i < p->n_exc;
+      if (o->plastic) {
+        double delta;
+        if (exc) {
+          delta = stdp * (pt * post * (4 - w) - 1.05 * pq * a * w);
+        } else {
+          delta = inh * (a * (pq - alpha) + pt * post);
+          delta *= q < p->n_exc ? 1.0 : 0.0;
+        }
+        w += delta;
+        if (exc) {
+          double x = (tgt - o->rate64[q]) / tgt * dt / tau_s;
+          x = x < -.001 ? -.001 : (x > .001 ? .001 : x);
+          w *= exp(x);
+        }
+        const double hi = exc ? 4.0 : 12.0;
+        w = w < .01 ? .01 : w;
+        w = w > hi ? hi : w;
+      }
+      o->coact64[e] = o->coact64[e] * slow + (1 - slow) * pot * post;
+      o->usage64[e] = o->usage64[e] * slow + (1 - slow) * a * 1000 / dt;
+      o->pre_tr64[e] = pt + a;
+      o->pot_tr64[e] = pot + a;
+      o->w64[e] = w0 < 0 ? -w : w;
+    }
+  }
+  for (int32_t i = 0; i < p->n; ++i) o->post_tr64[i] = o->post_tr64[i] * decay + (spk[i] ? 1.0 : 0.0);
+}
+
+/* Arrival flags of this tick from the spike history (contact e: its
+ * presynaptic cell's spike `delay` ticks ago). */
+static void arrivals_of(const on_net *o, const uint8_t *hist, int64_t t, uint8_t *arr) {
+  for (int32_t i = 0; i < o->p.n; ++i)
+    for (int64_t e = o->row[i]; e < o->row[i + 1]; ++e)
+      arr[e] = hist[(size_t)((t - o->delay[e]) & (RING - 1)) * o->p.n + i];
+}
+
+/* One learning step with caller-given arrivals (per stored contact) and
+ * spikes (per cell), as biology.py's learn() probe; fp64 != 0 selects the
+ * double state.  Test infrastructure for the reference's known-answer tests. */
+void on_learn_probe(void *h, const uint8_t *arr, const uint8_t *spk, int fp64) {
+  on_net *o = (on_net *)h;
+  if (fp64) learn64(o, arr, spk);
+  else learn32(o, arr, spk);
+}
+
+/* Plasticity state in the stored contact order (by presynaptic cell, stable
+ * in input order): weights, traces; per cell the post trace and the rate.
+ * Any pointer may be NULL. */
+void on_get_plasticity(void *h, float *w, float *pre_tr, float *pot_tr, float *coact, float *usage,
+                       float *post_tr, float *rate) {
+  on_net *o = (on_net *)h;
+  const size_t E = (size_t)o->nnz, N = (size_t)o->p.n;
+  if (w) memcpy(w, o->w, E * 4);
+  if (o->pre_tr) {
+    if (pre_tr) memcpy(pre_tr, o->pre_tr, E * 4);
+    if (pot_tr) memcpy(pot_tr, o->pot_tr, E * 4);
+    if (coact) memcpy(coact, o->coact, E * 4);
+    if (usage) memcpy(usage, o->usage, E * 4);
+    if (post_tr) memcpy(post_tr, o->post_tr, N * 4);
+    if (rate) memcpy(rate, o->rate, N * 4);
+  }
+}
+
+void on_get_plasticity64(void *h, double *w, double *pre_tr, double *pot_tr, double *coact, double *usage,
+                         double *post_tr, double *rate) {
+  on_net *o = (on_net *)h;
+  const size_t E = (size_t)o->nnz, N = (size_t)o->p.n;
+  if (w) memcpy(w, o->w64, E * 8);
+  if (o->pre_tr64) {
+    if (pre_tr) memcpy(pre_tr, o->pre_tr64, E * 8);
+    if (pot_tr) memcpy(pot_tr, o->pot_tr64, E * 8);
+    if (coact) memcpy(coact, o->coact64, E * 8);
+    if (usage) memcpy(usage, o->usage64, E * 8);
+    if (post_tr) memcpy(post_tr, o->post_tr64, N * 8);
+    if (rate) memcpy(rate, o->rate64, N * 8);
+  }
+}
+
 static float decay_f(float dt, float tau) { return (float)exp(-(double)dt / (double)tau); }
 
 /* fp32 ticks.  spikes: [ticks][ceil(n/32)] bit words (may be NULL);
@@ -229,6 +427,18 @@ int on_run(void *h, int ticks, uint32_t *spikes, int64_t *counts) {
       if (s && exc) a = a + p->adapt_inc;
       o->v[i] = v; o->a[i] = a; o->ge[i] = ge; o->gi[i] = gi; o->ref[i] = ref;
       fired[i] = (uint8_t)s;
+    }
+    if (o->pre_tr) { /* rate (biology.py:167-168), learn (:170), spike history (:174) */
+      const on_lc c = lc_of(o);
+      for (int32_t i = 0; i < n; ++i) {
+        o->rate[i] = o->rate[i] * c.slow;
+        if (fired[i]) o->rate[i] = o->rate[i] + c.rate_inc;
+      }
+      uint8_t *arr = (uint8_t *)malloc((size_t)(o->nnz ? o->nnz : 1));
+      arrivals_of(o, o->hist, t, arr);
+      learn32(o, arr, fired);
+      free(arr);
+      memcpy(o->hist + (size_t)(t & (RING - 1)) * n, fired, (size_t)n);
     }
     if (spikes) memset(spikes + (size_t)k * words, 0, words * 4);
     for (int32_t i = 0; i < n; ++i) {
@@ -294,6 +504,17 @@ int on_run64(void *h, int ticks, const double *current, uint32_t *spikes, double
       if (ge_out) ge_out[(size_t)k * n + i] = ge;
       if (gi_out) gi_out[(size_t)k * n + i] = gi;
     }
+    if (o->pre_tr64) {
+      for (int32_t i = 0; i < n; ++i) {
+        o->rate64[i] *= exp(-dt / 1000.0);
+        o->rate64[i] += (1 - exp(-dt / 1000.0)) * (fired[i] ? 1.0 : 0.0) * 1000 / dt;
+      }
+      uint8_t *arr = (uint8_t *)malloc((size_t)(o->nnz ? o->nnz : 1));
+      arrivals_of(o, o->hist64, t, arr);
+      learn64(o, arr, fired);
+      free(arr);
+      memcpy(o->hist64 + (size_t)(t & (RING - 1)) * n, fired, (size_t)n);
+    }
     if (spikes) memset(spikes + (size_t)k * words, 0, words * 4);
     for (int32_t i = 0; i < n; ++i) {
       if (!fired[i]) continue;
@@ -326,6 +547,7 @@ void on_set_state64(void *h, const double *v, const double *a, const double *ge,
  * result -- is identical to on_run).  Used as the timed CPU baseline. */
 int on_run_mt(void *h, int ticks, int64_t *counts) {
   on_net *o = (on_net *)h;
+  if (o->pre_tr) return -1; /* plasticity runs in on_run */
   const on_params *p = &o->p;
   const int32_t n = p->n;
   const float dE = decay_f(p->dt, p->tau_e), dI = decay_f(p->dt, p->tau_i), dA = decay_f(p->dt, p->tau_a);
