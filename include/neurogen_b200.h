@@ -182,7 +182,17 @@ typedef struct {
                                    below 65,536 neurons, else 2.                */
   int32_t part_rank, part_world; /* neuron row-partition: this rank owns neurons
                                    [rank*n/world, (rank+1)*n/world); 0/1 = whole */
-  int32_t reserved[4];
+  /* Learning (biology.py:182-218): pair STDP with soft bounds on E contacts, the
+   * inhibitory rule on I->E contacts, multiplicative synaptic scaling toward
+   * target_hz, weights clipped to [0.01, 4] (E) / [0.01, 12] (I); the tick's
+   * emissions carry the learned weights.  Needs fp32 weights, CSR storage and an
+   * unpartitioned network; runs the split launch shape, one tick after another. */
+  int32_t plasticity;           /* 0 frozen synapses (default), 1 learn every tick */
+  float stdp_rate;              /* .005 */
+  float inhibitory_rate;        /* .002 */
+  float target_hz;              /* 5 */
+  float scaling_tau_ms;         /* 100000 */
+  int32_t reserved[3];
 } ng_net_config;
 
 /* Fill `cfg` with the biology.py defaults (BiologyConfig, biology.py:19-77;
@@ -258,6 +268,16 @@ int ng_net_run(void *net, int ticks, uint32_t *spikes, int64_t *counts);
 /* Running totals since creation: totals[0] = spikes, totals[1] = synaptic
  * events delivered (host array of 2).  Synchronises the network's stream. */
 int ng_net_stats(void *net, int64_t *totals);
+
+/* Learning state of a plasticity network (cfg.plasticity = 1): per contact, in
+ * the order of ng_net_export, the pre trace, potential trace, coactivity and
+ * usage (Hz); per neuron the postsynaptic trace and the rate (Hz), as
+ * biology.py's BiologicalNetwork holds them.  The weights themselves come from
+ * ng_net_export.  NULL pointers skip; -1 if the network does not learn.  No
+ * counterpart in the reference's C ABI (its learning network is biology.py). */
+int ng_net_plasticity_state(void *net, float *pre_trace, float *potential_trace,
+                            float *coactivity, float *usage, float *post_trace,
+                            float *rate);
 
 /* Device-side run on a caller stream (NULL = the network's stream): no host
  * copies, no synchronisation.  d_spikes/d_counts may be NULL. */

@@ -50,6 +50,12 @@ void ng_net_default_config(ng_net_config *c) {
   c->launch = 0;
   c->part_rank = 0;
   c->part_world = 0;
+  // BiologyConfig learning defaults (biology.py:31-34); off unless asked for.
+  c->plasticity = 0;
+  c->stdp_rate = .005f;
+  c->inhibitory_rate = .002f;
+  c->target_hz = 5.f;
+  c->scaling_tau_ms = 100000.f;
 }
 
 void *ng_net_create(const ng_net_config *cfg) {
@@ -131,6 +137,16 @@ int ng_net_launch_kind(void *net) {
   const Network &w = *static_cast<Network *>(net);
   if (w.resident()) return w.resident_plan().pipe ? 4 : 3;
   return w.split() ? 2 : 1;
+}
+
+int ng_net_plasticity_state(void *net, float *pre_trace, float *potential_trace, float *coactivity, float *usage,
+                            float *post_trace, float *rate) {
+  return guarded([&] {
+    if (!net) throw std::invalid_argument("Null network");
+    auto &n = *static_cast<Network *>(net);
+    std::lock_guard<std::mutex> lock(n.mutex);
+    n.plasticity_state(pre_trace, potential_trace, coactivity, usage, post_trace, rate);
+  });
 }
 
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay, float *weight) {

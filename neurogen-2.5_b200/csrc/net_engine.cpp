@@ -121,6 +121,15 @@ void validate_config(const ng_net_config &c) {
     throw std::invalid_argument("launch must be 0 (auto), 1 (fused), 2 (split) or 3 (resident)");
   if (c.launch == 3 && c.part_world > 1)
     throw std::invalid_argument("The resident launch needs an unpartitioned network");
+  if (c.plasticity != 0 && c.plasticity != 1) throw std::invalid_argument("plasticity must be 0 or 1");
+  if (c.plasticity) {
+    if (!(c.stdp_rate >= 0) || !(c.inhibitory_rate >= 0) || !std::isfinite(c.stdp_rate) ||
+        !std::isfinite(c.inhibitory_rate) || !(c.target_hz > 0) || !std::isfinite(c.target_hz) ||
+        !(c.scaling_tau_ms > 0) || !std::isfinite(c.scaling_tau_ms))
+      throw std::invalid_argument("Learning rates must be finite and nonnegative, target_hz and scaling_tau_ms positive");
+    if (c.part_world > 1 || c.storage != 0 || c.weight_kind != NG_W_LOGNORMAL_F32 || c.launch == 1 || c.launch == 3)
+      throw std::invalid_argument("Learning needs fp32 weights, CSR storage, an unpartitioned network and the split launch");
+  }
   switch (c.topology) {
   case NG_TOPO_ERDOS_RENYI:
     if (!(c.p_connect >= 0 && c.p_connect <= 1)) throw std::invalid_argument("p_connect must be in [0, 1]");
@@ -739,7 +748,8 @@ void Network::init_state(const void *nccl_id, int max_delay) {
   // the presynaptic groups); tick.
   // Resident launch (persistent kernel, state in shared memory) when asked
   // for, or by default when the network qualifies and fits.
-  if (world_ == 1 && (c.launch == 3 || c.launch == 0)) resident_ = plan_resident(max_delay, c.launch == 3);
+  if (world_ == 1 && !c.plasticity && (c.launch == 3 || c.launch == 0))
+    resident_ = plan_resident(max_delay, c.launch == 3);
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
   const size_t groups = std::max({pre_groups, (N + kNetBlock - 1) / kNetBlock, size_t(resident_ ? res_.ctas : 0)});
   const size_t bm_words = pre_groups * (kNetBlock / 32);
@@ -765,7 +775,8 @@ void Network::init_state(const void *nccl_id, int max_delay) {
   if (const char *v = std::getenv("NEUROGEN_PUSH_CHUNK")) d.push_chunk = std::atoi(v) == 8 ? 8 : 16;
   // Small networks: one fused launch per tick; large or partitioned: split
   // membrane / push, with the bitmask all-gather between them.
-  split_ = world_ > 1 || c.launch == 2 || (c.launch == 0 && n_ >= 65536);
+  split_ = world_ > 1 || c.launch == 2 || (c.launch == 0 && n_ >= 65536) || c.plasticity;
+  if (c.plasticity) init_learning(bm_words);
   if (world_ > 1) {
     if (!nccl_id) throw std::invalid_argument("A partitioned network needs an NCCL unique id");
     ncclUniqueId id;
@@ -774,6 +785,73 @@ void Network::init_state(const void *nccl_id, int max_delay) {
   }
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   if (resident_) build_owner_blocks();
+}
+
+// Learning buffers (biology.py:182-218): per CSR entry (padding included, never
+// read) four traces, per neuron the post trace and the rate, the spike history,
+// all zero; constants of the fp32 contract (oracle/net_oracle.c lc_of).
+void Network::init_learning(size_t bm_words) {
+  const ng_net_config &c = cfg;
+  if (!dev_.row || dev_.bsr || (dev_.w_half && nnz_ > 0))
+    throw std::invalid_argument("Learning needs fp32 weights in CSR storage");
+  long long entries = 0;
+  NGB_CUDA(cudaMemcpy(&entries, dev_.row + n_pre_, 8, cudaMemcpyDeviceToHost));
+  const size_t E = size_t(std::max<long long>(entries, 1)), N = size_t(n_);
+  for (DeviceBuffer *b : {&pre_tr_, &pot_tr_, &coact_, &usage_}) {
+    b->reset(E * 4);
+    NGB_CUDA(cudaMemset(b->as<void>(), 0, E * 4));
+  }
+  for (DeviceBuffer *b : {&post_tr_, &rate_}) {
+    b->reset(N * 4);
+    NGB_CUDA(cudaMemset(b->as<void>(), 0, N * 4));
+  }
+  hist_.reset(size_t(kRingSlots) * bm_words * 4);
+  NGB_CUDA(cudaMemset(hist_.as<void>(), 0, size_t(kRingSlots) * bm_words * 4));
+  NetDev &d = dev_;
+  d.pre_tr = pre_tr_.as<float>();
+  d.pot_tr = pot_tr_.as<float>();
+  d.coact = coact_.as<float>();
+  d.usage = usage_.as<float>();
+  d.post_tr = post_tr_.as<float>();
+  d.rate = rate_.as<float>();
+  d.hist = hist_.as<uint32_t>();
+  d.learn_weights = 1;
+  const double dt = c.dt_ms;
+  d.l_decay = float(std::exp(-dt / 20.0));
+  d.l_slow = float(std::exp(-dt / 1000.0));
+  d.l_oms = float(1.0 - std::exp(-dt / 1000.0));
+  d.l_rate_inc = float((1.0 - std::exp(-dt / 1000.0)) * 1000.0 / dt);
+  d.l_per_ms = float(1000.0 / dt);
+  d.l_alpha = float(2.0 * double(c.target_hz) * .020);
+  d.l_stdp = c.stdp_rate;
+  d.l_inh = c.inhibitory_rate;
+  d.l_target = c.target_hz;
+  d.l_tau_s = c.scaling_tau_ms;
+  d.l_dt = float(dt);
+}
+
+// Learning state in the order of export_edges (CSR order, padding skipped).
+void Network::plasticity_state(float *pre_tr, float *pot_tr, float *coact, float *usage, float *post_tr,
+                               float *rate) {
+  NGB_CUDA(cudaSetDevice(device));
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  if (!dev_.pre_tr) throw std::invalid_argument("The network does not learn (plasticity = 0)");
+  std::vector<long long> row(size_t(n_pre_) + 1);
+  NGB_CUDA(cudaMemcpy(row.data(), row_.as<void>(), row.size() * 8, cudaMemcpyDeviceToHost));
+  const size_t E = size_t(row[n_pre_]);
+  std::vector<float> w(E), buf(E);
+  if (E) NGB_CUDA(cudaMemcpy(w.data(), w_.as<void>(), E * 4, cudaMemcpyDeviceToHost));
+  const float *src[4] = {dev_.pre_tr, dev_.pot_tr, dev_.coact, dev_.usage};
+  float *dst[4] = {pre_tr, pot_tr, coact, usage};
+  for (int k = 0; k < 4; ++k) {
+    if (!dst[k] || !E) continue;
+    NGB_CUDA(cudaMemcpy(buf.data(), src[k], E * 4, cudaMemcpyDeviceToHost));
+    size_t j = 0;
+    for (size_t e = 0; e < E; ++e)
+      if (w[e] != 0.f) dst[k][j++] = buf[e];
+  }
+  if (post_tr) NGB_CUDA(cudaMemcpy(post_tr, dev_.post_tr, size_t(n_) * 4, cudaMemcpyDeviceToHost));
+  if (rate) NGB_CUDA(cudaMemcpy(rate, dev_.rate, size_t(n_) * 4, cudaMemcpyDeviceToHost));
 }
 
 // Resident launch plan: CTAs of P neurons (a multiple of 32, at least 256 so
@@ -902,6 +980,7 @@ void Network::launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned 
                           cudaStream_t st) {
   if (split_) {
     launch_membrane(t, parity, spikes_row, counts_row, st);
+    if (dev_.pre_tr) launch_net_learn(dev_, t, st); // learn before the tick's emissions
     launch_net_push(dev_, t, counts_row, 0, st);
   } else {
     launch_net_fused(dev_, t, spikes_row, counts_row, st);
@@ -918,7 +997,8 @@ void Network::launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned 
 // ring slot t+2 and rewrites tick t's bitmask buffer.
 void Network::capture_graph() {
   const long long *td = tick_dev_.as<long long>();
-  if (split_ && !stream_rest_) {
+  const bool pipelined = split_ && !dev_.pre_tr; // learning: each tick's push before the next learns
+  if (pipelined && !stream_rest_) {
     NGB_CUDA(cudaStreamCreateWithFlags(&stream_rest_, cudaStreamNonBlocking));
     for (cudaEvent_t *e : {&ev_fork_, &ev_alif_, &ev_rest_[0], &ev_rest_[1], &ev_join_})
       NGB_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
@@ -926,7 +1006,7 @@ void Network::capture_graph() {
   cudaGraph_t g = nullptr;
   NGB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   try {
-    if (split_) {
+    if (pipelined) {
       NGB_CUDA(cudaEventRecord(ev_fork_, stream));
       NGB_CUDA(cudaStreamWaitEvent(stream_rest_, ev_fork_, 0));
       for (int k = 0; k < kGraphTicks; ++k) {

@@ -84,6 +84,8 @@ public:
   void enqueue(int ticks, uint32_t *d_spikes, unsigned long long *d_counts, cudaStream_t st);
   void run_host(int ticks, uint32_t *spikes, int64_t *counts);
   void stats(int64_t *totals);
+  // Learning networks: per-contact traces in export order, per-neuron post trace and rate.
+  void plasticity_state(float *pre_tr, float *pot_tr, float *coact, float *usage, float *post_tr, float *rate);
   bool split() const { return split_; }
   bool resident() const { return resident_; }
   const ResidentDev &resident_plan() const { return res_; }
@@ -104,6 +106,8 @@ private:
   DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
   DeviceBuffer rec_spikes_, rec_counts_;
   DeviceBuffer bitmask_, totals_, tick_dev_;
+  DeviceBuffer pre_tr_, pot_tr_, coact_, usage_, post_tr_, rate_, hist_; // learning
+  void init_learning(size_t bm_words);
   bool split_ = false;
   cudaGraphExec_t graph_ = nullptr;
   static constexpr int kGraphTicks = 64;

@@ -214,13 +214,91 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   const int i = blockIdx.x * TB + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const bool s = i < d.n ? alif_update(d, t, i) : false;
+  if (d.rate && i < d.n) {
+    // Learning networks: the rate trace (biology.py:167-168).
+    float r = __fmul_rn(d.rate[i], d.l_slow);
+    if (s) r = __fadd_rn(r, d.l_rate_inc);
+    d.rate[i] = r;
+  }
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
   if (lane == 0 && base < d.n) {
     d.bitmask[(t & 1) * d.bm_stride + ((d.base + base) >> 5)] = fired;
+    if (d.hist) d.hist[(t & (kRingSlots - 1)) * d.bm_stride + (base >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + kTotalsStride * (size_t)blockIdx.x, counts);
+}
+
+
+// ---------------------------------------------------------------------------
+// Learning (plasticity networks): biology.py:182-218 in the fp32 contract of
+// oracle/net_oracle.c (learn32): every operation rounded as written, the
+// constants the reference's expressions in double rounded once.  One warp per
+// presynaptic row: lanes 0..15 read the row's spike bit of the last 16 ticks
+// from the history (bit j: tick t - j), so a contact of delay d sees its
+// arrival as bit d; the lanes then take the row's contacts 32 at a time.
+// Zero-weight entries (row padding) are not contacts.  The post trace of every
+// neuron is decayed and advanced after all contacts have read it (k_net_post).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(TB) k_net_learn(NetDev d, TickRef tr) {
+  const long long t = tick_of(tr);
+  const int lane = threadIdx.x & 31;
+  const int p = blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (p >= d.n_pre) return;
+  uint32_t bit = 0;
+  if (lane < kRingSlots) bit = (d.hist[((t - lane) & (kRingSlots - 1)) * d.bm_stride + (p >> 5)] >> (p & 31)) & 1u;
+  const unsigned past = __ballot_sync(0xffffffffu, bit != 0); // bit j: spike at tick t - j
+  const uint32_t *now = d.hist + (t & (kRingSlots - 1)) * d.bm_stride;
+  const bool exc = p < d.n_exc;
+  float *w32 = static_cast<float *>(const_cast<void *>(d.w));
+  const long long e1 = d.row[p + 1];
+  for (long long e = d.row[p] + lane; e < e1; e += 32) {
+    const float w0 = w32[e];
+    if (w0 == 0.f) continue;
+    const uint32_t word = d.syn[e];
+    const int q = (int)(word & kPostMask);
+    const int dly = (int)(word >> 28) + 1;
+    const float a = ((past >> dly) & 1u) ? 1.f : 0.f;
+    const float post = ((now[q >> 5] >> (q & 31)) & 1u) ? 1.f : 0.f;
+    const float pt = __fmul_rn(d.pre_tr[e], d.l_decay);
+    const float pot = __fmul_rn(d.pot_tr[e], d.l_decay);
+    const float pq = __fmul_rn(d.post_tr[q], d.l_decay);
+    float w = fabsf(w0);
+    if (d.learn_weights) {
+      float delta;
+      if (exc) {
+        delta = __fmul_rn(d.l_stdp, __fsub_rn(__fmul_rn(__fmul_rn(pt, post), __fsub_rn(4.f, w)),
+                                              __fmul_rn(__fmul_rn(__fmul_rn(1.05f, pq), a), w)));
+      } else {
+        delta = __fmul_rn(d.l_inh, __fadd_rn(__fmul_rn(a, __fsub_rn(pq, d.l_alpha)), __fmul_rn(pt, post)));
+        delta = __fmul_rn(delta, q < d.n_exc ? 1.f : 0.f);
+      }
+      w = __fadd_rn(w, delta);
+      if (exc) {
+        float x = __fdiv_rn(__fmul_rn(__fdiv_rn(__fsub_rn(d.l_target, d.rate[q]), d.l_target), d.l_dt), d.l_tau_s);
+        x = x < -.001f ? -.001f : (x > .001f ? .001f : x);
+        w = __fmul_rn(w, ng_expf(x));
+      }
+      const float hi = exc ? 4.f : 12.f;
+      w = w < .01f ? .01f : w;
+      w = w > hi ? hi : w;
+    }
+    d.coact[e] = __fadd_rn(__fmul_rn(d.coact[e], d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, pot), post));
+    d.usage[e] = __fadd_rn(__fmul_rn(d.usage[e], d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, a), d.l_per_ms));
+    d.pre_tr[e] = __fadd_rn(pt, a);
+    d.pot_tr[e] = __fadd_rn(pot, a);
+    w32[e] = w0 < 0.f ? -w : w;
+  }
+}
+
+__global__ void __launch_bounds__(TB) k_net_post(NetDev d, TickRef tr) {
+  const long long t = tick_of(tr);
+  const int i = blockIdx.x * TB + threadIdx.x;
+  if (i >= d.n) return;
+  const uint32_t *now = d.hist + (t & (kRingSlots - 1)) * d.bm_stride;
+  const float s = ((now[i >> 5] >> (i & 31)) & 1u) ? 1.f : 0.f;
+  d.post_tr[i] = __fadd_rn(__fmul_rn(d.post_tr[i], d.l_decay), s);
 }
 
 // CTA b pushes the spikes of presynaptic neurons [32*SPANW*b, 32*SPANW*(b+1)):
@@ -299,6 +377,11 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
   const int blocks = (d.n + TB - 1) / TB;
   if (d.bsr) k_net_alif<true><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
   else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
+}
+
+void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s) {
+  if (d.n_pre > 0) k_net_learn<<<(d.n_pre + WARPS - 1) / WARPS, TB, 0, s>>>(d, t);
+  if (d.n > 0) k_net_post<<<(d.n + TB - 1) / TB, TB, 0, s>>>(d, t);
 }
 
 template <bool BSR, int SPANW, int CH>

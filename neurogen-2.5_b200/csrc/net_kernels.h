@@ -50,6 +50,14 @@ struct NetDev {
   uint32_t drive_thr;
   unsigned long long drive_key;
   int ref_ticks;
+  // Learning (plasticity networks; null pointers otherwise): per CSR entry the
+  // pre trace, potential trace, coactivity and usage; per neuron the post trace
+  // and the rate; the spike bitmask of the last kRingSlots ticks [16][bm_stride].
+  float *pre_tr, *pot_tr, *coact, *usage, *post_tr, *rate;
+  uint32_t *hist;
+  int learn_weights; // 1: weights learn (0: traces only)
+  // Constants of the fp32 contract (the reference's expressions in double, rounded once).
+  float l_decay, l_slow, l_oms, l_rate_inc, l_per_ms, l_alpha, l_stdp, l_inh, l_target, l_tau_s, l_dt;
 };
 
 // Which tick a launch computes: *t_dev + k when t_dev is set (graph replay
@@ -68,6 +76,10 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
                      cudaStream_t s);
 // seg: 0 whole rows, 1 delay-1 segments only, 2 delay>=2 segments only.
 void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s);
+// Learning of tick t (plasticity networks), after k_net_alif and before the
+// push: every contact's weight and traces (biology.py:182-218), then every
+// neuron's post trace.
+void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s);
 constexpr int kTotalsStride = 3;
 constexpr int kNetBlock = 256; // neurons per membrane CTA
 void launch_set_tick(long long *t_dev, long long value, cudaStream_t s);

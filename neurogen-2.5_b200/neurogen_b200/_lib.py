@@ -29,7 +29,7 @@ EXPORTS = (
     'ng_net_synapses', 'ng_net_export', 'ng_net_set_state', 'ng_net_get_state', 'ng_net_run',
     'ng_net_run_device', 'ng_topology_create', 'ng_topology_destroy', 'ng_topology_synapses',
     'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static', 'ng_net_launch_kind',
-    'ng_net_create_partitioned', 'ng_nccl_unique_id', 'ng_math_eval',
+    'ng_net_create_partitioned', 'ng_nccl_unique_id', 'ng_math_eval', 'ng_net_plasticity_state',
 )
 
 
@@ -47,7 +47,9 @@ class NetConfig(ct.Structure):
         ('tau_adapt_ms', ct.c_float), ('adapt_inc_pa', ct.c_float), ('bias_pa', ct.c_float),
         ('drive_kind', ct.c_int32), ('drive_p', ct.c_float), ('drive_ns', ct.c_float),
         ('storage', ct.c_int32), ('launch', ct.c_int32), ('part_rank', ct.c_int32),
-        ('part_world', ct.c_int32), ('reserved', ct.c_int32 * 4),
+        ('part_world', ct.c_int32), ('plasticity', ct.c_int32), ('stdp_rate', ct.c_float),
+        ('inhibitory_rate', ct.c_float), ('target_hz', ct.c_float), ('scaling_tau_ms', ct.c_float),
+        ('reserved', ct.c_int32 * 3),
     ]
 
 
@@ -137,6 +139,8 @@ def library():
     lib.ng_nccl_unique_id.restype = ci
     lib.ng_net_stats.argtypes = [vp, I64]
     lib.ng_net_stats.restype = ci
+    lib.ng_net_plasticity_state.argtypes = [vp, vp, vp, vp, vp, vp, vp]
+    lib.ng_net_plasticity_state.restype = ci
     lib.ng_topology_create.argtypes = [cfgp]
     lib.ng_topology_create.restype = vp
     lib.ng_topology_destroy.argtypes = [vp]

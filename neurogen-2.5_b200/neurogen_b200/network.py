@@ -137,6 +137,16 @@ class Network:
         """The resident launch's tick: 'pipelined' or 'serial' (None for the other launch shapes)."""
         return {3: 'serial', 4: 'pipelined'}.get(self.lib.ng_net_launch_kind(self.h))
 
+    def plasticity_state(self):
+        """Learning state (plasticity networks): per contact in export() order the pre trace,
+        potential trace, coactivity and usage; per neuron the post trace and the rate (Hz)."""
+        m, n = self.synapses, self.n
+        per_edge = {k: np.empty(m, np.float32) for k in ('pre_trace', 'potential_trace', 'coactivity', 'usage')}
+        post_tr, rate = np.empty(n, np.float32), np.empty(n, np.float32)
+        self._check(self.lib.ng_net_plasticity_state(self.h, *[x.ctypes.data for x in per_edge.values()],
+                                                     post_tr.ctypes.data, rate.ctypes.data))
+        return dict(per_edge, post_trace=post_tr, rate=rate)
+
     def export(self):
         m = self.synapses
         pre, post, delay = (np.empty(m, np.int32) for _ in range(3))

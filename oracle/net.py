@@ -44,7 +44,8 @@ DEFAULTS = dict(n=1024, n_exc=819, topology=0, p_connect=0.02, fanin=512, bsr_bl
                 cap_exc_pf=200.0, cap_inh_pf=100.0, g_leak_ns=10.0, e_leak_mv=-65.0, e_inh_mv=-80.0,
                 v_thresh_mv=-50.0, v_reset_mv=-65.0, t_ref_ms=2.0, tau_exc_ms=5.0, tau_inh_ms=10.0,
                 tau_adapt_ms=200.0, adapt_inc_pa=15.0, bias_pa=0.0, drive_kind=0, drive_p=0.02, drive_ns=4.0,
-                storage=0, launch=0, part_rank=0, part_world=0)
+                storage=0, launch=0, part_rank=0, part_world=0, plasticity=0, stdp_rate=.005,
+                inhibitory_rate=.002, target_hz=5.0, scaling_tau_ms=1e5)
 
 
 def config(**overrides):

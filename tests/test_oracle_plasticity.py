@@ -152,3 +152,15 @@ def test_fp32_contract_follows_fp64_with_learning():
     w32, w64 = a.plasticity_state()['weight'], b.plasticity_state(fp64=True)['weight']
     assert (w32 != w).sum() > 1000
     np.testing.assert_allclose(w32, w64, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize('bad', [dict(weight_kind=1), dict(storage=1, topology=2, weight_kind=1),
+                                 dict(launch='resident'), dict(launch='fused'), dict(target_hz=0.0),
+                                 dict(stdp_rate=-1.0), dict(plasticity=2)])
+def test_learning_configuration_is_checked(bad):
+    """The engine refuses learning where its arithmetic contract does not hold (fp16 weights,
+    block storage, the fused and resident launch shapes) and invalid rates, on the host."""
+    from neurogen_b200.network import Topology
+    cfg = default_config(**dict(dict(n=256, n_exc=200, plasticity=1), **bad))
+    with pytest.raises(ValueError):
+        Topology(cfg)
