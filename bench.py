@@ -8,6 +8,8 @@ Workloads (seeded synthetic inputs of the benchmark configurations):
   bsr262k   the same with the 16x16 block matrix (128 block-columns per block-row, 25% fill).
   tick8k    isolated tick: N=8,192 Erdos-Renyi 2%, lognormal fp32 weights, Bernoulli(0.02)
             conductance drive; one step = 1,000 ticks.  metric ticks/s.
+  learn8k   the same network learning every tick (biology.py's STDP, inhibitory rule, synaptic
+            scaling and traces on every contact; split launch shape).
   partitioned4m  N=4,194,304, fan-in 1,000, fp16, imposed Bernoulli(0.01), 1,000 ticks a step;
             under torchrun the neurons are row-partitioned over the ranks with a per-tick NCCL
             all-gather of the spike bitmask (one network: strong scaling).
@@ -43,16 +45,18 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 METRIC_TICKS = 'ticks/sec (synaptic events/sec alongside)'
 METRIC_TOKENS = 'tokens/sec at BC-250 profile'
-TICK_WORKLOADS = ('tick262k', 'bsr262k', 'tick8k', 'partitioned4m')
+TICK_WORKLOADS = ('tick262k', 'bsr262k', 'tick8k', 'learn8k', 'partitioned4m')
 LANG_WORKLOADS = ('bc250', 'sessions')
 WORKLOAD_NAMES = {'tick262k': 'scaled_tick_262144_csr', 'bsr262k': 'scaled_tick_262144_bsr16',
-                  'tick8k': 'isolated_tick_8192', 'partitioned4m': 'partitioned_4194304_fanin1000',
+                  'tick8k': 'isolated_tick_8192', 'learn8k': 'isolated_tick_8192_learning',
+                  'partitioned4m': 'partitioned_4194304_fanin1000',
                   'bc250': 'bc250_batch1', 'sessions': 'bc250_sessions256'}
-TICKS_PER_STEP = {'tick262k': 10000, 'bsr262k': 10000, 'tick8k': 1000, 'partitioned4m': 1000}
+TICKS_PER_STEP = {'tick262k': 10000, 'bsr262k': 10000, 'tick8k': 1000, 'learn8k': 1000, 'partitioned4m': 1000}
 TOKENS_PER_STEP = {'bc250': 512, 'sessions': 64}
 SESSIONS = 256
 # Steps and warm-up steps of the workloads that follow the headline (bounded run time).
-EXTRA_STEPS = {'tick262k': 3, 'bsr262k': 3, 'tick8k': 10, 'partitioned4m': 3, 'bc250': 3, 'sessions': 5}
+EXTRA_STEPS = {'tick262k': 3, 'bsr262k': 3, 'tick8k': 10, 'learn8k': 5, 'partitioned4m': 3, 'bc250': 3,
+               'sessions': 5}
 L2_BYTES = 126e6
 
 
@@ -213,6 +217,8 @@ def oracle_tick_config(name, rate, n_override=0):
         return on.scaled_262k('csr', rate=rate)
     if name == 'bsr262k':
         return on.scaled_262k('bsr', rate=rate)
+    if name == 'learn8k':
+        return dict(on.isolated_8k(), plasticity=1, launch=2)
     return on.isolated_8k()
 
 
@@ -230,6 +236,8 @@ def tick_config_dict(name, c, world, ticks):
                       'Bernoulli(%g) conductance drive of %g nS' % (c['drive_p'], c['drive_ns'])),
             'weights': 'fp16' if c['weight_kind'] == 1 else 'fp32', 'delays': [c['delay_min'], c['delay_max']],
             'synapses': synapses if topo != 0 else f'~{synapses}',
+            'learning': ('STDP + inhibitory rule + synaptic scaling + traces every tick'
+                         if c.get('plasticity') else None),
             'l2': 'inputs larger than L2' if synapses * 6 > L2_BYTES else 'network fits in L2; L2 flushed between steps',
             'parallelism': (f'rows{world} + NCCL bitmask all-gather' if part and world > 1 else
                             'one GPU' if part else f'replicas{world}')}
@@ -251,7 +259,7 @@ def engine_config(c):
 # ---------------------------------------------------------------------------
 # Tick-network workloads (our arm).
 # ---------------------------------------------------------------------------
-def tick_bytes(cfg, spikes, events, held=None):
+def tick_bytes(cfg, spikes, events, held=None, contacts=0):
     """Algorithmic DRAM bytes of one tick, the roofline numerator.
 
     Per neuron: the four fp32 state values (V, adaptation, g_E, g_I) read and written (32 B),
@@ -265,7 +273,12 @@ def tick_bytes(cfg, spikes, events, held=None):
     per_neuron = held * 48 + held / 8
     if cfg.storage == 1:
         return per_neuron + spikes * cfg.bsr_blocks * 36
-    return per_neuron + events * (4 + wbytes + 1)
+    learning = 0
+    if cfg.plasticity and contacts:
+        # Every contact every tick: index read, weight and four traces read and written (44 B);
+        # every neuron: post trace and rate read and written (16 B) and its history bit.
+        learning = contacts * 44 + held * 16 + held / 8
+    return per_neuron + events * (4 + wbytes + 1) + learning
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per tick from one ncu capture of the
@@ -347,7 +360,7 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
     t_max = dist.max(elapsed)
     total_ticks = ticks * steps
     held = cfg.n // dist.world if part else cfg.n
-    b_tick = tick_bytes(cfg, spikes / total_ticks, events / total_ticks, held)
+    b_tick = tick_bytes(cfg, spikes / total_ticks, events / total_ticks, held, contacts=synapses)
     pk, src = peaks()
     if part:  # one network over all ranks: sum the ranks' bytes, compare with all their peaks
         b_tick = dist.sum(b_tick)
@@ -423,7 +436,20 @@ def oracle_network(name, oc):
     if name == 'partitioned4m':
         scale = 16
         oc = dict(oc, n=oc['n'] // scale, n_exc=oc['n_exc'] // scale)
-    return on.NetOracle(oc, *on.generate(oc)), scale
+    orc = on.NetOracle(oc, *on.generate(oc))
+    if oc.get('plasticity'):
+        orc.set_plasticity(True, stdp_rate=oc['stdp_rate'], inhibitory_rate=oc['inhibitory_rate'],
+                           target_hz=oc['target_hz'], scaling_tau_ms=oc['scaling_tau_ms'])
+    return orc, scale
+
+
+def oracle_ticks(orc, oc, ticks):
+    """Run the checker: OpenMP over all host cores, or one thread for a learning network (the
+    oracle's learning step is single-threaded)."""
+    if oc.get('plasticity'):
+        orc.run(ticks)
+    else:
+        orc.run_mt(ticks)
 
 
 def cpu_baseline_ticks(name, oc, budget_s):
@@ -431,16 +457,17 @@ def cpu_baseline_ticks(name, oc, budget_s):
     t0 = time.time()
     orc, scale = oracle_network(name, oc)
     build_s = time.time() - t0
-    orc.run_mt(2)
+    oracle_ticks(orc, oc, 2)
     done, el = 0, 0.0
-    chunk = 5 if oc['n'] > 100000 else 100
+    chunk = 5 if oc['n'] > 100000 else (20 if oc.get('plasticity') else 100)
     while el < budget_s:
         t1 = time.time()
-        orc.run_mt(chunk)
+        oracle_ticks(orc, oc, chunk)
         el += time.time() - t1
         done += chunk
-    cores = int(os.environ.get('OMP_NUM_THREADS', multiprocessing.cpu_count()))
-    sample = (f'{done} ticks of the same network (oracle/net_oracle.c on_run_mt, OpenMP), {el:.1f} s; '
+    cores = 1 if oc.get('plasticity') else int(os.environ.get('OMP_NUM_THREADS', multiprocessing.cpu_count()))
+    how = 'on_run with learning, one thread' if oc.get('plasticity') else 'on_run_mt, OpenMP'
+    sample = (f'{done} ticks of the same network (oracle/net_oracle.c {how}), {el:.1f} s; '
               f'network generation {build_s:.1f} s excluded')
     if scale > 1:
         sample += f'; 1/{scale}-scale network, time per tick x{scale}'
@@ -645,19 +672,20 @@ def reference_record(name, args, world, steps, warmup):
     if name in TICK_WORKLOADS:
         oc = oracle_tick_config(name, args.rate)
         orc, scale = oracle_network(name, oc)
-        sample = 20 if oc['n'] > 100000 else 200
+        sample = 20 if oc['n'] > 100000 else (40 if oc.get('plasticity') else 200)
         for _ in range(warmup):
-            orc.run_mt(sample)
+            oracle_ticks(orc, oc, sample)
         t0 = time.time()
         for _ in range(steps):
-            orc.run_mt(sample)
+            oracle_ticks(orc, oc, sample)
         el = time.time() - t0
         value, unit = sample * steps / el / scale, 'ticks/s'
         ms_per_step = el / steps * 1e3 * scale / sample * TICKS_PER_STEP[name]
         config = tick_config_dict(name, oc, world, TICKS_PER_STEP[name])
         scaling = 'strong' if name == 'partitioned4m' else 'weak'
-        kind, threads = 'port', cores
-        desc = f'{sample} ticks per step (oracle/net_oracle.c, OpenMP on {cores} cores)'
+        kind, threads = 'port', (1 if oc.get('plasticity') else cores)
+        desc = (f'{sample} ticks per step (oracle/net_oracle.c with learning, one thread)' if oc.get('plasticity')
+                else f'{sample} ticks per step (oracle/net_oracle.c, OpenMP on {cores} cores)')
         if scale > 1:
             desc += f'; 1/{scale}-scale network (N={oc["n"] // scale:,}), time per tick x{scale}'
         metric = METRIC_TICKS
@@ -700,7 +728,7 @@ def reference_record(name, args, world, steps, warmup):
 
 
 def extras_for(headline):
-    return [w for w in ('bc250', 'sessions', 'tick8k', 'bsr262k', 'partitioned4m') if w != headline]
+    return [w for w in ('bc250', 'sessions', 'tick8k', 'learn8k', 'bsr262k', 'partitioned4m') if w != headline]
 
 
 def main():
