@@ -801,7 +801,7 @@ void Network::init_learning(size_t bm_words) {
     b->reset(E * 4);
     NGB_CUDA(cudaMemset(b->as<void>(), 0, E * 4));
   }
-  for (DeviceBuffer *b : {&post_tr_, &rate_}) {
+  for (DeviceBuffer *b : {&post_tr_, &rate_, &scale_}) {
     b->reset(N * 4);
     NGB_CUDA(cudaMemset(b->as<void>(), 0, N * 4));
   }
@@ -814,6 +814,7 @@ void Network::init_learning(size_t bm_words) {
   d.usage = usage_.as<float>();
   d.post_tr = post_tr_.as<float>();
   d.rate = rate_.as<float>();
+  d.scale = scale_.as<float>();
   d.hist = hist_.as<uint32_t>();
   d.learn_weights = 1;
   const double dt = c.dt_ms;

@@ -215,10 +215,15 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   const int lane = threadIdx.x & 31;
   const bool s = i < d.n ? alif_update(d, t, i) : false;
   if (d.rate && i < d.n) {
-    // Learning networks: the rate trace (biology.py:167-168).
+    // Learning networks: the rate trace (biology.py:167-168), and from it this
+    // tick's synaptic-scaling factor of the neuron's E contacts (:207-208),
+    // exp(clip((target - rate) / target * dt / tau, -.001, .001)).
     float r = __fmul_rn(d.rate[i], d.l_slow);
     if (s) r = __fadd_rn(r, d.l_rate_inc);
     d.rate[i] = r;
+    float x = __fdiv_rn(__fmul_rn(__fdiv_rn(__fsub_rn(d.l_target, r), d.l_target), d.l_dt), d.l_tau_s);
+    x = x < -.001f ? -.001f : (x > .001f ? .001f : x);
+    d.scale[i] = ng_expf(x);
   }
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
@@ -241,54 +246,75 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
 // Zero-weight entries (row padding) are not contacts.  The post trace of every
 // neuron is decayed and advanced after all contacts have read it (k_net_post).
 // ---------------------------------------------------------------------------
+// One contact's learning step (the fp32 contract); a = arrival, post = postsynaptic spike.
+__device__ __forceinline__ void learn_contact(const NetDev &d, bool exc, int q, float a, float post, float &w_io,
+                                              float &pre_tr, float &pot_tr, float &coact, float &usage) {
+  const float pt = __fmul_rn(pre_tr, d.l_decay);
+  const float pot = __fmul_rn(pot_tr, d.l_decay);
+  const float pq = __fmul_rn(d.post_tr[q], d.l_decay);
+  float w = fabsf(w_io);
+  if (d.learn_weights) {
+    float delta;
+    if (exc) {
+      delta = __fmul_rn(d.l_stdp, __fsub_rn(__fmul_rn(__fmul_rn(pt, post), __fsub_rn(4.f, w)),
+                                            __fmul_rn(__fmul_rn(__fmul_rn(1.05f, pq), a), w)));
+    } else {
+      delta = __fmul_rn(d.l_inh, __fadd_rn(__fmul_rn(a, __fsub_rn(pq, d.l_alpha)), __fmul_rn(pt, post)));
+      delta = __fmul_rn(delta, q < d.n_exc ? 1.f : 0.f);
+    }
+    w = __fadd_rn(w, delta);
+    if (exc) w = __fmul_rn(w, d.scale[q]); // the postsynaptic neuron's factor (k_net_alif)
+    const float hi = exc ? 4.f : 12.f;
+    w = w < .01f ? .01f : w;
+    w = w > hi ? hi : w;
+  }
+  coact = __fadd_rn(__fmul_rn(coact, d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, pot), post));
+  usage = __fadd_rn(__fmul_rn(usage, d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, a), d.l_per_ms));
+  pre_tr = __fadd_rn(pt, a);
+  pot_tr = __fadd_rn(pot, a);
+  w_io = w_io < 0.f ? -w : w;
+}
+
 __global__ void __launch_bounds__(TB) k_net_learn(NetDev d, TickRef tr) {
   const long long t = tick_of(tr);
-  const int lane = threadIdx.x & 31;
-  const int p = blockIdx.x * WARPS + (threadIdx.x >> 5);
-  if (p >= d.n_pre) return;
+  const int lane = threadIdx.x & 31, hl = lane & 15;
+  // Two presynaptic rows a warp, one a half-warp.
+  const int p = (blockIdx.x * WARPS + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const bool valid = p < d.n_pre;
   uint32_t bit = 0;
-  if (lane < kRingSlots) bit = (d.hist[((t - lane) & (kRingSlots - 1)) * d.bm_stride + (p >> 5)] >> (p & 31)) & 1u;
-  const unsigned past = __ballot_sync(0xffffffffu, bit != 0); // bit j: spike at tick t - j
+  if (valid) bit = (d.hist[((t - hl) & (kRingSlots - 1)) * d.bm_stride + (p >> 5)] >> (p & 31)) & 1u;
+  // bit j of `past`: the row's spike at tick t - j (j < 16).
+  const unsigned past = (__ballot_sync(0xffffffffu, bit != 0) >> (lane & 16)) & 0xFFFFu;
+  if (!valid) return;
   const uint32_t *now = d.hist + (t & (kRingSlots - 1)) * d.bm_stride;
   const bool exc = p < d.n_exc;
   float *w32 = static_cast<float *>(const_cast<void *>(d.w));
+  // Rows start and end on multiples of 8 entries: four contacts a lane, 16-byte accesses.
   const long long e1 = d.row[p + 1];
-  for (long long e = d.row[p] + lane; e < e1; e += 32) {
-    const float w0 = w32[e];
-    if (w0 == 0.f) continue;
-    const uint32_t word = d.syn[e];
-    const int q = (int)(word & kPostMask);
-    const int dly = (int)(word >> 28) + 1;
-    const float a = ((past >> dly) & 1u) ? 1.f : 0.f;
-    const float post = ((now[q >> 5] >> (q & 31)) & 1u) ? 1.f : 0.f;
-    const float pt = __fmul_rn(d.pre_tr[e], d.l_decay);
-    const float pot = __fmul_rn(d.pot_tr[e], d.l_decay);
-    const float pq = __fmul_rn(d.post_tr[q], d.l_decay);
-    float w = fabsf(w0);
-    if (d.learn_weights) {
-      float delta;
-      if (exc) {
-        delta = __fmul_rn(d.l_stdp, __fsub_rn(__fmul_rn(__fmul_rn(pt, post), __fsub_rn(4.f, w)),
-                                              __fmul_rn(__fmul_rn(__fmul_rn(1.05f, pq), a), w)));
-      } else {
-        delta = __fmul_rn(d.l_inh, __fadd_rn(__fmul_rn(a, __fsub_rn(pq, d.l_alpha)), __fmul_rn(pt, post)));
-        delta = __fmul_rn(delta, q < d.n_exc ? 1.f : 0.f);
-      }
-      w = __fadd_rn(w, delta);
-      if (exc) {
-        float x = __fdiv_rn(__fmul_rn(__fdiv_rn(__fsub_rn(d.l_target, d.rate[q]), d.l_target), d.l_dt), d.l_tau_s);
-        x = x < -.001f ? -.001f : (x > .001f ? .001f : x);
-        w = __fmul_rn(w, ng_expf(x));
-      }
-      const float hi = exc ? 4.f : 12.f;
-      w = w < .01f ? .01f : w;
-      w = w > hi ? hi : w;
+  for (long long e = d.row[p] + 4 * hl; e < e1; e += 64) {
+    float4 w4 = *reinterpret_cast<const float4 *>(w32 + e);
+    if (w4.x == 0.f && w4.y == 0.f && w4.z == 0.f && w4.w == 0.f) continue; // row padding
+    const uint4 s4 = *reinterpret_cast<const uint4 *>(d.syn + e);
+    float4 pr = *reinterpret_cast<const float4 *>(d.pre_tr + e);
+    float4 po = *reinterpret_cast<const float4 *>(d.pot_tr + e);
+    float4 co = *reinterpret_cast<const float4 *>(d.coact + e);
+    float4 us = *reinterpret_cast<const float4 *>(d.usage + e);
+    float *wv = &w4.x, *prv = &pr.x, *pov = &po.x, *cov = &co.x, *usv = &us.x;
+    const uint32_t words[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (wv[j] == 0.f) continue; // not a contact
+      const int q = (int)(words[j] & kPostMask);
+      const int dly = (int)(words[j] >> 28) + 1;
+      const float a = ((past >> dly) & 1u) ? 1.f : 0.f;
+      const float post = ((now[q >> 5] >> (q & 31)) & 1u) ? 1.f : 0.f;
+      learn_contact(d, exc, q, a, post, wv[j], prv[j], pov[j], cov[j], usv[j]);
     }
-    d.coact[e] = __fadd_rn(__fmul_rn(d.coact[e], d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, pot), post));
-    d.usage[e] = __fadd_rn(__fmul_rn(d.usage[e], d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, a), d.l_per_ms));
-    d.pre_tr[e] = __fadd_rn(pt, a);
-    d.pot_tr[e] = __fadd_rn(pot, a);
-    w32[e] = w0 < 0.f ? -w : w;
+    *reinterpret_cast<float4 *>(w32 + e) = w4;
+    *reinterpret_cast<float4 *>(d.pre_tr + e) = pr;
+    *reinterpret_cast<float4 *>(d.pot_tr + e) = po;
+    *reinterpret_cast<float4 *>(d.coact + e) = co;
+    *reinterpret_cast<float4 *>(d.usage + e) = us;
   }
 }
 
@@ -380,7 +406,7 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
 }
 
 void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s) {
-  if (d.n_pre > 0) k_net_learn<<<(d.n_pre + WARPS - 1) / WARPS, TB, 0, s>>>(d, t);
+  if (d.n_pre > 0) k_net_learn<<<(d.n_pre + 2 * WARPS - 1) / (2 * WARPS), TB, 0, s>>>(d, t);
   if (d.n > 0) k_net_post<<<(d.n + TB - 1) / TB, TB, 0, s>>>(d, t);
 }
 

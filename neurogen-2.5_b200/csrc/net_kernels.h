@@ -54,6 +54,7 @@ struct NetDev {
   // pre trace, potential trace, coactivity and usage; per neuron the post trace
   // and the rate; the spike bitmask of the last kRingSlots ticks [16][bm_stride].
   float *pre_tr, *pot_tr, *coact, *usage, *post_tr, *rate;
+  float *scale;   // per neuron, this tick: the synaptic-scaling factor of its E contacts
   uint32_t *hist;
   int learn_weights; // 1: weights learn (0: traces only)
   // Constants of the fp32 contract (the reference's expressions in double, rounded once).
