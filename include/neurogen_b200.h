@@ -245,12 +245,20 @@ int64_t ng_net_synapses(void *net);
  * serial tick, 4 resident with the pipelined tick; -1 on a null handle.  No counterpart in the reference (its isolated-tick network is
  * biology.py's NumPy loop). */
 int ng_net_launch_kind(void *net);
+
+/* How a partitioned network's ranks exchange each tick's spikes: 0 not
+ * partitioned, 1 NCCL all-gather, 2 one-sided stores into every rank's buffers
+ * over NVLink with tick-stamped flags (the default when every rank can map the
+ * others' memory; NEUROGEN_PEER_EXCHANGE=0 selects NCCL); -1 on a null handle.
+ * No counterpart in the reference. */
+int ng_net_exchange_kind(void *net);
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay,
                   float *weight);
 
 /* State: v, adapt, g_exc, g_inh (fp32 [n] each), refractory ticks (int32 [n]),
  * delay ring (int32 [16][n][2]) and the tick counter.  NULL pointers skip.
- * For a partitioned network n is this rank's neuron count. */
+ * For a partitioned network n is this rank's neuron count, and ng_net_set_state
+ * is collective (every rank calls it, with the same tick). */
 int ng_net_set_state(void *net, const float *v, const float *adapt,
                      const float *g_exc, const float *g_inh,
                      const int32_t *refractory, const int32_t *ring,

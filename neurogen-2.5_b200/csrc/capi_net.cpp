@@ -149,6 +149,12 @@ int ng_net_plasticity_state(void *net, float *pre_trace, float *potential_trace,
   });
 }
 
+int ng_net_exchange_kind(void *net) {
+  if (!net) return -1;
+  const Network &w = *static_cast<Network *>(net);
+  return w.exchange_kind();
+}
+
 int ng_net_export(void *net, int32_t *pre, int32_t *post, int32_t *delay, float *weight) {
   return guarded([&] {
     if (!net) throw std::invalid_argument("Null network");

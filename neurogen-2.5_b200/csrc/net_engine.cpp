@@ -753,15 +753,18 @@ void Network::init_state(const void *nccl_id, int max_delay) {
   const size_t pre_groups = (size_t(n_pre_) + kNetBlock - 1) / kNetBlock;
   const size_t groups = std::max({pre_groups, (N + kNetBlock - 1) / kNetBlock, size_t(resident_ ? res_.ctas : 0)});
   const size_t bm_words = pre_groups * (kNetBlock / 32);
-  bitmask_.reset(2 * bm_words * 4);
+  bitmask_.reset(3 * bm_words * 4);
   totals_.reset(groups * kTotalsStride * sizeof(unsigned long long));
   tick_dev_.reset(sizeof(long long));
-  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, 2 * bm_words * 4));
+  NGB_CUDA(cudaMemset(bitmask_.as<void>(), 0, 3 * bm_words * 4));
   NGB_CUDA(cudaMemset(totals_.as<void>(), 0, groups * kTotalsStride * sizeof(unsigned long long)));
   totals_pairs_ = groups;
   NGB_CUDA(cudaMemset(tick_dev_.as<void>(), 0, sizeof(long long)));
   d.bitmask = bitmask_.as<uint32_t>();
   d.bm_stride = int(bm_words);
+  d.bm_bufs = 2;
+  d.world = world_;
+  d.rank = rank_;
   d.totals = totals_.as<unsigned long long>();
   // Split push shape: a CTA scans 64 bitmask words (2,048 presynaptic neurons)
   // when the presynaptic population is large, so the grid follows the spikes
@@ -782,9 +785,124 @@ void Network::init_state(const void *nccl_id, int max_delay) {
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof id);
     nccl_check(nccl().CommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
+    NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    if (world_ <= 32) setup_peer_exchange(bm_words); // one waiting lane per rank
   }
-  NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  if (!stream) NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   if (resident_) build_owner_blocks();
+}
+
+// One-sided spike exchange of a partitioned network (the default when every
+// rank can map every other rank's memory; NEUROGEN_PEER_EXCHANGE=0 keeps the
+// NCCL all-gather).  Each rank allocates its three bitmask buffers and its flag
+// array in one block, shares the block's CUDA IPC handle with the others (one
+// NCCL all-gather of fixed-size records that also carry the device's UUID and
+// whether the rank wants the exchange), and maps theirs.  The decision is
+// collective: one rank that cannot take part, or two ranks on the same GPU
+// (whose waits could not run side by side), keeps every rank on NCCL.
+void Network::setup_peer_exchange(size_t bm_words) {
+  struct Record {
+    int32_t ok;
+    unsigned char uuid[16];
+    cudaIpcMemHandle_t handle;
+    int32_t pad[3];
+  };
+  const char *env = std::getenv("NEUROGEN_PEER_EXCHANGE");
+  const size_t bm_bytes = 3 * bm_words * 4, flag_at = (bm_bytes + 255) & ~size_t(255);
+  xbuf_.reset(flag_at + size_t(world_) * 8);
+  NGB_CUDA(cudaMemset(xbuf_.as<void>(), 0, flag_at + size_t(world_) * 8));
+  Record mine{};
+  mine.ok = !(env && std::string(env) == "0");
+  cudaDeviceProp prop{};
+  NGB_CUDA(cudaGetDeviceProperties(&prop, device));
+  std::memcpy(mine.uuid, &prop.uuid, 16);
+  if (mine.ok && cudaIpcGetMemHandle(&mine.handle, xbuf_.as<void>()) != cudaSuccess) {
+    (void)cudaGetLastError();
+    mine.ok = 0;
+  }
+  auto gather = [&](const void *rec, size_t bytes, std::vector<unsigned char> &all) {
+    DeviceBuffer buf(bytes * world_);
+    NGB_CUDA(cudaMemcpy(buf.as<unsigned char>() + bytes * rank_, rec, bytes, cudaMemcpyHostToDevice));
+    nccl_check(nccl().AllGather(buf.as<unsigned char>() + bytes * rank_, buf.as<void>(), bytes, ncclChar, comm_,
+                                stream),
+               "ncclAllGather (peer exchange set-up)");
+    NGB_CUDA(cudaStreamSynchronize(stream));
+    all.resize(bytes * world_);
+    NGB_CUDA(cudaMemcpy(all.data(), buf.as<void>(), all.size(), cudaMemcpyDeviceToHost));
+  };
+  std::vector<unsigned char> all;
+  gather(&mine, sizeof mine, all);
+  std::vector<Record> recs(world_);
+  std::memcpy(recs.data(), all.data(), all.size());
+  bool ok = true;
+  for (int r = 0; r < world_; ++r) {
+    ok = ok && recs[r].ok;
+    for (int q = 0; q < r; ++q) ok = ok && std::memcmp(recs[r].uuid, recs[q].uuid, 16) != 0;
+  }
+  std::vector<void *> base(world_, nullptr);
+  base[rank_] = xbuf_.as<void>();
+  int32_t opened = 1;
+  if (ok) {
+    for (int r = 0; r < world_ && opened; ++r) {
+      if (r == rank_) continue;
+      if (cudaIpcOpenMemHandle(&base[r], recs[r].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        (void)cudaGetLastError();
+        base[r] = nullptr;
+        opened = 0;
+      }
+    }
+  }
+  // Second round: every rank mapped every other's block, or all fall back.
+  std::vector<unsigned char> all_opened;
+  gather(&opened, sizeof opened, all_opened);
+  for (int r = 0; r < world_; ++r) ok = ok && reinterpret_cast<int32_t *>(all_opened.data())[r];
+  if (!ok) {
+    for (int r = 0; r < world_; ++r)
+      if (r != rank_ && base[r]) cudaIpcCloseMemHandle(base[r]);
+    xbuf_.reset(0);
+    return;
+  }
+  peer_bases_ = base;
+  std::vector<uint32_t *> bm(world_);
+  std::vector<unsigned long long *> fl(world_);
+  for (int r = 0; r < world_; ++r) {
+    bm[r] = static_cast<uint32_t *>(base[r]);
+    fl[r] = reinterpret_cast<unsigned long long *>(static_cast<unsigned char *>(base[r]) + flag_at);
+  }
+  peer_bm_ = upload_vec(bm);
+  peer_flag_ = upload_vec(fl);
+  xctl_.reset(32); // [0..2] CTA counters, [3] error word, [4..5] epoch (u64)
+  NGB_CUDA(cudaMemset(xctl_.as<void>(), 0, 32));
+  NetDev &d = dev_;
+  d.bitmask = bm[rank_];
+  d.bm_bufs = 3;
+  d.peer_bm = peer_bm_.as<uint32_t *>();
+  d.peer_flag = peer_flag_.as<unsigned long long *>();
+  d.xflag = fl[rank_];
+  d.xcount = xctl_.as<unsigned>();
+  d.xerr = reinterpret_cast<int *>(xctl_.as<unsigned>() + 3);
+  d.xepoch = reinterpret_cast<const unsigned long long *>(xctl_.as<unsigned>() + 4);
+}
+
+// A state load on a peer-exchange network is collective: every rank's earlier
+// ticks are done (their kernels precede this all-gather on their streams), and
+// the epoch advances, so flags stamped before the load never satisfy a wait
+// after it, whatever tick the load sets.
+void Network::exchange_epoch() {
+  DeviceBuffer tmp(size_t(world_) * 4);
+  nccl_check(nccl().AllGather(tmp.as<unsigned char>() + 4 * rank_, tmp.as<void>(), 4, ncclChar, comm_, stream),
+             "ncclAllGather (state load)");
+  NGB_CUDA(cudaStreamSynchronize(stream));
+  ++epoch_;
+  NGB_CUDA(cudaMemcpy(const_cast<unsigned long long *>(dev_.xepoch), &epoch_, 8, cudaMemcpyHostToDevice));
+}
+
+// Raises the peer exchange's error (a wait for another rank's spikes that ran out).
+void Network::check_exchange() {
+  if (!dev_.xerr) return;
+  int err = 0;
+  NGB_CUDA(cudaMemcpy(&err, dev_.xerr, 4, cudaMemcpyDeviceToHost));
+  if (err) throw std::runtime_error("Peer spike exchange: a wait for another rank's spikes timed out");
 }
 
 // Learning buffers (biology.py:182-218): per CSR entry (padding included, never
@@ -953,6 +1071,8 @@ void Network::check_resident() {
 
 Network::~Network() {
   if (graph_) cudaGraphExecDestroy(graph_); // before the communicator its NCCL nodes use
+  for (size_t r = 0; r < peer_bases_.size(); ++r)
+    if (int(r) != rank_ && peer_bases_[r]) cudaIpcCloseMemHandle(peer_bases_[r]);
   if (comm_) nccl().CommDestroy(comm_);
   for (cudaEvent_t e : {ev_fork_, ev_alif_, ev_rest_[0], ev_rest_[1], ev_join_})
     if (e) cudaEventDestroy(e);
@@ -967,10 +1087,17 @@ void Network::launch_membrane(TickRef t, int parity, uint32_t *spikes_row, unsig
                               cudaStream_t st) {
   launch_net_alif(dev_, t, world_ > 1 ? nullptr : spikes_row, counts_row, st);
   if (world_ > 1) {
-    uint32_t *bm = bitmask_.as<uint32_t>() + size_t(parity) * size_t(dev_.bm_stride);
-    const size_t words = size_t(n_) / 32;
-    nccl_check(nccl().AllGather(bm + size_t(base_) / 32, bm, words, ncclUint32, comm_, st), "ncclAllGather");
-    if (spikes_row)
+    uint32_t *bm;
+    if (dev_.peer_bm) {
+      // One-sided: the ranks' kernels have stored their slices here; wait for their flags.
+      launch_net_xwait(dev_, t, st);
+      bm = dev_.bitmask + size_t(t.t_dev ? 0 : t.k % 3) * size_t(dev_.bm_stride);
+    } else {
+      bm = bitmask_.as<uint32_t>() + size_t(parity) * size_t(dev_.bm_stride);
+      const size_t words = size_t(n_) / 32;
+      nccl_check(nccl().AllGather(bm + size_t(base_) / 32, bm, words, ncclUint32, comm_, st), "ncclAllGather");
+    }
+    if (spikes_row) // recorded runs only: the tick number is known here
       NGB_CUDA(cudaMemcpyAsync(spikes_row, bm, size_t(n_pre_) / 32 * 4, cudaMemcpyDeviceToDevice, st));
   }
 }
@@ -1045,6 +1172,7 @@ void Network::stats(int64_t *totals) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaDeviceSynchronize());
   check_resident();
+  check_exchange();
   const size_t groups = totals_pairs_;
   std::vector<unsigned long long> g(groups * kTotalsStride);
   NGB_CUDA(cudaMemcpy(g.data(), totals_.as<void>(), g.size() * 8, cudaMemcpyDeviceToHost));
@@ -1105,12 +1233,14 @@ void Network::set_state(const float *v, const float *a, const float *ge, const f
   if (ring) NGB_CUDA(cudaMemcpy(ring_.as<void>(), ring, size_t(kRingSlots) * N * 8, cudaMemcpyHostToDevice));
   if (tick < 0) throw std::invalid_argument("tick must be non-negative");
   tick_ = tick;
+  if (dev_.peer_bm) exchange_epoch();
 }
 
 void Network::get_state(float *v, float *a, float *ge, float *gi, int32_t *ref, int32_t *ring, int64_t *tick) {
   NGB_CUDA(cudaSetDevice(device));
   NGB_CUDA(cudaStreamSynchronize(stream));
   check_resident();
+  check_exchange();
   const size_t N = size_t(n_);
   if (v) NGB_CUDA(cudaMemcpy(v, v_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
   if (a) NGB_CUDA(cudaMemcpy(a, a_.as<void>(), N * 4, cudaMemcpyDeviceToHost));
@@ -1173,6 +1303,7 @@ void Network::run_host(int ticks, uint32_t *spikes, int64_t *counts) {
                                cudaMemcpyDeviceToHost, stream));
     NGB_CUDA(cudaStreamSynchronize(stream));
     check_resident();
+    check_exchange();
   }
   NGB_CUDA(cudaStreamSynchronize(stream));
 }

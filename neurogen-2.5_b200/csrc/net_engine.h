@@ -87,6 +87,7 @@ public:
   // Learning networks: per-contact traces in export order, per-neuron post trace and rate.
   void plasticity_state(float *pre_tr, float *pot_tr, float *coact, float *usage, float *post_tr, float *rate);
   bool split() const { return split_; }
+  int exchange_kind() const { return world_ > 1 ? (dev_.peer_bm ? 2 : 1) : 0; }
   bool resident() const { return resident_; }
   const ResidentDev &resident_plan() const { return res_; }
 
@@ -108,6 +109,13 @@ private:
   DeviceBuffer bitmask_, totals_, tick_dev_;
   DeviceBuffer pre_tr_, pot_tr_, coact_, usage_, post_tr_, rate_, scale_, hist_; // learning
   void init_learning(size_t bm_words);
+  // One-sided spike exchange (partitioned networks).
+  DeviceBuffer xbuf_, peer_bm_, peer_flag_, xctl_;
+  std::vector<void *> peer_bases_;
+  void setup_peer_exchange(size_t bm_words);
+  void check_exchange();
+  void exchange_epoch();
+  unsigned long long epoch_ = 0;
   bool split_ = false;
   cudaGraphExec_t graph_ = nullptr;
   static constexpr int kGraphTicks = 64;

@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(TB) k_net_fused(NetDev d, TickRef tr, uint32_t
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane; // fused launches are unpartitioned: base 0
   if (lane == 0 && base < d.n) {
-    d.bitmask[(t & 1) * d.bm_stride + (base >> 5)] = fired;
+    d.bitmask[(t % d.bm_bufs) * d.bm_stride + (base >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   unsigned long long events = 0;
@@ -228,11 +228,50 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
   if (lane == 0 && base < d.n) {
-    d.bitmask[(t & 1) * d.bm_stride + ((d.base + base) >> 5)] = fired;
+    const size_t at = (size_t)(t % d.bm_bufs) * d.bm_stride + ((d.base + base) >> 5);
+    if (d.peer_bm) {
+      for (int r = 0; r < d.world; ++r) d.peer_bm[r][at] = fired; // every rank's copy, over NVLink
+    } else {
+      d.bitmask[at] = fired;
+    }
     if (d.hist) d.hist[(t & (kRingSlots - 1)) * d.bm_stride + (base >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + kTotalsStride * (size_t)blockIdx.x, counts);
+  if (d.peer_bm && threadIdx.x == 0) {
+    // The CTA's stores (ordered before thread 0 by the barrier in
+    // add_block_count) reach every rank before its count; the last CTA then
+    // raises this rank's flag for tick t in every rank.
+    __threadfence_system();
+    const int b = (int)(t % 3);
+    if (atomicAdd(d.xcount + b, 1u) == gridDim.x - 1) {
+      d.xcount[b] = 0u;
+      __threadfence_system();
+      const unsigned long long stamp = (*d.xepoch << 40) | ((unsigned long long)t + 1ull);
+      for (int r = 0; r < d.world; ++r)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(d.peer_flag[r] + d.rank), "l"(stamp) : "memory");
+    }
+  }
+}
+
+__global__ void k_net_xwait(NetDev d, TickRef tr) {
+  const long long t = tick_of(tr);
+  const int r = threadIdx.x;
+  if (r >= d.world || *(volatile int *)d.xerr) return;
+  const unsigned long long target = (*d.xepoch << 40) | ((unsigned long long)t + 1ull);
+  unsigned long long start;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+  for (unsigned spin = 0; spin < (1u << 30); ++spin) {
+    unsigned long long f;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(f) : "l"(d.xflag + r) : "memory");
+    if (f >= target) return;
+    if ((spin & 63u) == 63u) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - start > 2000000000ull || *(volatile int *)d.xerr) break;
+    }
+  }
+  atomicExch(d.xerr, 1);
 }
 
 
@@ -341,7 +380,7 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
   __shared__ unsigned item_mask[BSR ? SPAN / 16 : 1];
   __shared__ int n_items;
   const long long t = tick_of(tr);
-  const uint32_t *bitmask = d.bitmask + (t & 1) * d.bm_stride;
+  const uint32_t *bitmask = d.bitmask + (t % d.bm_bufs) * d.bm_stride;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int base = blockIdx.x * SPAN;
   if (warp == 0) {
@@ -404,6 +443,8 @@ void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned 
   if (d.bsr) k_net_alif<true><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
   else k_net_alif<false><<<blocks, TB, 0, s>>>(d, t, spikes_out, counts);
 }
+
+void launch_net_xwait(const NetDev &d, TickRef t, cudaStream_t s) { k_net_xwait<<<1, 32, 0, s>>>(d, t); }
 
 void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s) {
   if (d.n_pre > 0) k_net_learn<<<(d.n_pre + 2 * WARPS - 1) / (2 * WARPS), TB, 0, s>>>(d, t);

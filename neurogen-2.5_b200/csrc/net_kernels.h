@@ -34,8 +34,21 @@ struct NetDev {
   float *v, *a, *ge, *gi;
   int *ref;
   int2 *ring;
-  uint32_t *bitmask;            // spike words of the whole network, two buffers (tick parity)
+  uint32_t *bitmask;            // spike words of the whole network, bm_bufs buffers (by t % bm_bufs)
   int bm_stride;                // words per buffer
+  int bm_bufs;                  // 2; 3 with the peer exchange
+  // Peer exchange of a partitioned network (one-sided, over NVLink; null:
+  // NCCL all-gather): every rank's bitmask buffers and flag array mapped here
+  // ([world], this rank's own at [rank]); flag[r] = 1 + the last tick whose
+  // whole slice rank r has stored into this rank's buffers, in the low 40 bits;
+  // the exchange epoch (advanced by every collective ng_net_set_state) above.
+  uint32_t *const *peer_bm;
+  unsigned long long *const *peer_flag;
+  unsigned long long *xflag;    // this rank's flag array [world]
+  unsigned *xcount;             // [3]: CTAs of k_net_alif done with tick t's stores (by t % 3)
+  int *xerr;                    // 1: a wait for a peer's flag ran out
+  const unsigned long long *xepoch; // the exchange epoch (device memory, read by the kernels)
+  int world, rank;
   int push_span_words;          // split push: bitmask words a CTA scans (8 or 64)
   int push_chunk;               // split push: synapses a lane takes a pass (8 or 16)
   // Running counters since creation, three per 256-neuron group: [g][0]
@@ -75,6 +88,9 @@ void launch_net_fused(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned
 // each 256-neuron group by one CTA.
 void launch_net_alif(const NetDev &d, TickRef t, uint32_t *spikes_out, unsigned long long *counts,
                      cudaStream_t s);
+// Peer exchange: wait (bounded, 2 s) until every rank's slice of tick t has
+// arrived; on a timeout *xerr = 1 and later waits return at once.
+void launch_net_xwait(const NetDev &d, TickRef t, cudaStream_t s);
 // seg: 0 whole rows, 1 delay-1 segments only, 2 delay>=2 segments only.
 void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s);
 // Learning of tick t (plasticity networks), after k_net_alif and before the

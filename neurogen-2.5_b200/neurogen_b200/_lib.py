@@ -30,6 +30,7 @@ EXPORTS = (
     'ng_net_run_device', 'ng_topology_create', 'ng_topology_destroy', 'ng_topology_synapses',
     'ng_topology_export', 'ng_net_create_topology', 'ng_net_stats', 'ng_step_static', 'ng_net_launch_kind',
     'ng_net_create_partitioned', 'ng_nccl_unique_id', 'ng_math_eval', 'ng_net_plasticity_state',
+    'ng_net_exchange_kind',
 )
 
 
@@ -141,6 +142,8 @@ def library():
     lib.ng_net_stats.restype = ci
     lib.ng_net_plasticity_state.argtypes = [vp, vp, vp, vp, vp, vp, vp]
     lib.ng_net_plasticity_state.restype = ci
+    lib.ng_net_exchange_kind.argtypes = [vp]
+    lib.ng_net_exchange_kind.restype = ci
     lib.ng_topology_create.argtypes = [cfgp]
     lib.ng_topology_create.restype = vp
     lib.ng_topology_destroy.argtypes = [vp]

@@ -133,6 +133,11 @@ class Network:
         return {1: 'fused', 2: 'split', 3: 'resident', 4: 'resident'}[self.lib.ng_net_launch_kind(self.h)]
 
     @property
+    def exchange(self):
+        """How a partitioned network's ranks exchange spikes: None, 'nccl' or 'peer'."""
+        return {0: None, 1: 'nccl', 2: 'peer'}[self.lib.ng_net_exchange_kind(self.h)]
+
+    @property
     def resident_tick(self):
         """The resident launch's tick: 'pipelined' or 'serial' (None for the other launch shapes)."""
         return {3: 'serial', 4: 'pipelined'}.get(self.lib.ng_net_launch_kind(self.h))

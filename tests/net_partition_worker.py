@@ -35,18 +35,24 @@ def main():
     dist.broadcast_object_list(ids, src=0)
     net = Network.partitioned(config(rank, world), ids[0])
     spikes, counts = net.run(60)
-    net.run(100, record=False)          # graph path with the all-gather captured
+    snap = net.get_state()              # tick 60
+    mid, _ = net.run(30)
+    net.run(100, record=False)          # graph path with the exchange captured
     tail, _ = net.run(5)
     st = net.get_state()
-    np.savez(out / f'rank{rank}.npz', spikes=spikes, counts=counts, tail=tail, stats=np.array(net.stats()),
-             **{k: st[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')})
+    stats = np.array(net.stats())
+    net.set_state(**snap)               # collective: every rank rewinds to tick 60
+    again, _ = net.run(30)
+    np.savez(out / f'rank{rank}.npz', spikes=spikes, counts=counts, mid=mid, tail=tail, again=again, stats=stats,
+             exchange=np.array(net.exchange), **{k: st[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')})
     if rank == 0:
         full = Network(config(0, 0))
         fs, fc = full.run(60)
+        fm, _ = full.run(30)
         full.run(100, record=False)
         ft, _ = full.run(5)
         fst = full.get_state()
-        np.savez(out / 'full.npz', spikes=fs, counts=fc, tail=ft, stats=np.array(full.stats()),
+        np.savez(out / 'full.npz', spikes=fs, counts=fc, mid=fm, tail=ft, stats=np.array(full.stats()),
                  **{k: fst[k] for k in ('v', 'a', 'ge', 'gi', 'ref', 'ring')})
     dist.barrier()
     net.close()

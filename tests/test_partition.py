@@ -81,8 +81,13 @@ def test_two_gloo_ranks_generate_disjoint_partitions(tmp_path):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason='needs two GPUs')
-def test_two_gpu_partition_equals_whole_network(tmp_path):
-    env = dict(os.environ, MASTER_ADDR='127.0.0.1', NCCL_NVLS_ENABLE='0')
+@pytest.mark.parametrize('exchange', ['peer', 'nccl'])
+def test_two_gpu_partition_equals_whole_network(tmp_path, exchange):
+    """Two ranks over NVLink with the one-sided peer exchange (default) or the NCCL all-gather:
+    every rank's whole-network raster equals the unpartitioned network's (recorded ticks, after
+    100 graph-replayed ticks, and again after a collective state load rewinds both ranks)."""
+    env = dict(os.environ, MASTER_ADDR='127.0.0.1', NCCL_NVLS_ENABLE='0',
+               NEUROGEN_PEER_EXCHANGE='1' if exchange == 'peer' else '0')
     cmd = ['timeout', '-k', '30', '300', sys.executable, '-m', 'torch.distributed.run', '--nnodes=1',
            '--nproc-per-node=2', '--master-addr', '127.0.0.1', '--master-port', '29643',
            str(ROOT / 'tests' / 'net_partition_worker.py'), str(tmp_path)]
@@ -91,8 +96,11 @@ def test_two_gpu_partition_equals_whole_network(tmp_path):
     full = np.load(tmp_path / 'full.npz')
     ranks = [np.load(tmp_path / f'rank{r}.npz') for r in range(2)]
     for r in ranks:
+        assert str(r['exchange']) == exchange
         assert np.array_equal(r['spikes'], full['spikes'])   # whole-network raster on every rank
+        assert np.array_equal(r['mid'], full['mid'])
         assert np.array_equal(r['tail'], full['tail'])       # after 100 graph-replayed ticks
+        assert np.array_equal(r['again'], full['mid'])       # rewound to tick 60 and run again
     assert full['counts'][:, 0].sum() > 1000
     assert sum(int(r['stats'][0]) for r in ranks) == int(full['stats'][0])
     assert sum(int(r['stats'][1]) for r in ranks) == int(full['stats'][1])
