@@ -298,14 +298,16 @@ def tick_traffic(workload, mode, rate):
 
 KERNEL_OF_LAUNCH = {'fused': 'k_net_fused', 'split': 'tick = k_net_alif + k_net_push',
                     'resident': 'k_net_resident (persistent, serial tick, 2,048 ticks a launch)',
-                    'resident-pipelined': 'k_net_pipe (persistent, pipelined tick, 2,048 ticks a launch)'}
+                    'resident-pipelined': 'k_net_pipe (persistent, pipelined tick, 2,048 ticks a launch)',
+                    'split-learning': 'tick = k_net_alif + k_net_learn + k_net_post + k_net_push'}
 
 
 def tick_launches(mode, ticks):
     """Kernels the engine launches for one run of `ticks` ticks without per-tick outputs."""
-    if mode == 'resident':
+    if mode.startswith('resident'):
         return -(-ticks // 2048)
-    per_tick = 1 if mode == 'fused' else 3
+    # split: membrane, delay-1 push, delay>=2 push; learning: membrane, learn, post trace, push
+    per_tick = 1 if mode == 'fused' else 4 if mode == 'split-learning' else 3
     graphs = ticks // 64
     return graphs * (64 * per_tick + 1) + (ticks - graphs * 64) * per_tick + (1 if graphs else 0)
 
@@ -339,7 +341,8 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
         synapses = net.synapses
     setup_s = time.time() - t0
     mode = net.launch
-    shape = 'resident-pipelined' if net.resident_tick == 'pipelined' else mode
+    shape = ('resident-pipelined' if net.resident_tick == 'pipelined' else
+             'split-learning' if cfg.plasticity else mode)
     stream = torch.cuda.Stream()  # explicit stream: the engine enqueues on exactly this one
 
     def step():
@@ -381,7 +384,7 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
                                  if not part else None),
                      'traffic_unit': 'bytes/tick (ncu, scaled by spike rate)', 'bytes_per_tick': b_tick,
                      'kernel': KERNEL_OF_LAUNCH[shape], 'peak_source': src},
-        'gpu_launches': tick_launches(mode, ticks) * steps,
+        'gpu_launches': tick_launches(shape, ticks) * steps,
         'clocks': clk.summary(),
     }
     if not args.no_e2e:
@@ -648,15 +651,21 @@ def partition_parity(dist):
     mine = np.array(net.stats(), np.float64)
     tot = torch.from_numpy(mine).cuda()
     dist.pg.all_reduce(tot)
+    # per-tick counts of a rank cover its own neurons' spikes and the events onto them: sum over ranks
+    tick_counts = torch.from_numpy(counts.astype(np.float64)).cuda()
+    dist.pg.all_reduce(tick_counts)
+    counts = tick_counts.cpu().numpy().astype(np.int64)
+    exchange = net.exchange
     net.close()
     ok = True
     detail = {}
     if dist.rank == 0:
         full = Network(default_config(**kw))
         fs, fc = full.run(100)
-        ok = (np.array_equal(spikes, fs) and np.array_equal(counts[:, 0], fc[:, 0]) and
+        ok = (np.array_equal(spikes, fs) and np.array_equal(counts, fc) and
               tuple(int(x) for x in tot.cpu().numpy()) == full.stats())
-        detail = {'ticks': 100, 'n': kw['n'], 'spikes': int(fc[:, 0].sum()), 'ranks': dist.world}
+        detail = {'ticks': 100, 'n': kw['n'], 'spikes': int(fc[:, 0].sum()), 'ranks': dist.world,
+                  'exchange': exchange}
         full.close()
     flag = torch.tensor([1.0 if ok else 0.0], device='cuda')
     dist.pg.all_reduce(flag, op=dist.pg.ReduceOp.MIN)

@@ -871,17 +871,16 @@ void Network::setup_peer_exchange(size_t bm_words) {
   }
   peer_bm_ = upload_vec(bm);
   peer_flag_ = upload_vec(fl);
-  xctl_.reset(32); // [0..2] CTA counters, [3] error word, [4..5] epoch (u64)
-  NGB_CUDA(cudaMemset(xctl_.as<void>(), 0, 32));
+  xctl_.reset(16); // [0] error word, [2..3] epoch (u64)
+  NGB_CUDA(cudaMemset(xctl_.as<void>(), 0, 16));
   NetDev &d = dev_;
   d.bitmask = bm[rank_];
   d.bm_bufs = 3;
   d.peer_bm = peer_bm_.as<uint32_t *>();
   d.peer_flag = peer_flag_.as<unsigned long long *>();
   d.xflag = fl[rank_];
-  d.xcount = xctl_.as<unsigned>();
-  d.xerr = reinterpret_cast<int *>(xctl_.as<unsigned>() + 3);
-  d.xepoch = reinterpret_cast<const unsigned long long *>(xctl_.as<unsigned>() + 4);
+  d.xerr = xctl_.as<int>();
+  d.xepoch = reinterpret_cast<const unsigned long long *>(xctl_.as<unsigned>() + 2);
 }
 
 // A state load on a peer-exchange network is collective: every rank's earlier

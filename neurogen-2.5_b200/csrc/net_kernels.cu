@@ -227,38 +227,38 @@ __global__ void __launch_bounds__(TB) k_net_alif(NetDev d, TickRef tr, uint32_t 
   }
   const unsigned fired = __ballot_sync(0xffffffffu, s);
   const int base = i - lane;
+  __shared__ uint32_t words_s[WARPS];
   if (lane == 0 && base < d.n) {
-    const size_t at = (size_t)(t % d.bm_bufs) * d.bm_stride + ((d.base + base) >> 5);
-    if (d.peer_bm) {
-      for (int r = 0; r < d.world; ++r) d.peer_bm[r][at] = fired; // every rank's copy, over NVLink
-    } else {
-      d.bitmask[at] = fired;
-    }
+    if (d.peer_bm) words_s[threadIdx.x >> 5] = fired;
+    else d.bitmask[(size_t)(t % d.bm_bufs) * d.bm_stride + ((d.base + base) >> 5)] = fired;
     if (d.hist) d.hist[(t & (kRingSlots - 1)) * d.bm_stride + (base >> 5)] = fired;
     if (spikes_out) spikes_out[base >> 5] = fired;
   }
   add_block_count(lane == 0 ? __popc(fired) : 0, d.totals + kTotalsStride * (size_t)blockIdx.x, counts);
-  if (d.peer_bm && threadIdx.x == 0) {
-    // The CTA's stores (ordered before thread 0 by the barrier in
-    // add_block_count) reach every rank before its count; the last CTA then
-    // raises this rank's flag for tick t in every rank.
-    __threadfence_system();
-    const int b = (int)(t % 3);
-    if (atomicAdd(d.xcount + b, 1u) == gridDim.x - 1) {
-      d.xcount[b] = 0u;
+  if (d.peer_bm) {
+    // The CTA's words (after the barrier in add_block_count) into every
+    // rank's buffer: thread j stores word j % WARPS to rank j / WARPS, so each
+    // rank gets one contiguous 32-byte piece; each storing thread fences its
+    // store system-wide before the CTA ends (k_net_xwait raises the flags
+    // once the whole kernel has ended).
+    const int j = threadIdx.x, w = j % WARPS, r = j / WARPS;
+    const int first = blockIdx.x * TB + w * 32;
+    if (r < d.world && first < d.n) {
+      d.peer_bm[r][(size_t)(t % d.bm_bufs) * d.bm_stride + ((d.base + first) >> 5)] = words_s[w];
       __threadfence_system();
-      const unsigned long long stamp = (*d.xepoch << 40) | ((unsigned long long)t + 1ull);
-      for (int r = 0; r < d.world; ++r)
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(d.peer_flag[r] + d.rank), "l"(stamp) : "memory");
     }
   }
 }
 
+// Runs after this rank's k_net_alif of tick t has ended (stream order), whose
+// threads fenced their stores system-wide: lane r raises this rank's flag in
+// rank r, then waits for rank r's flag here.
 __global__ void k_net_xwait(NetDev d, TickRef tr) {
   const long long t = tick_of(tr);
   const int r = threadIdx.x;
   if (r >= d.world || *(volatile int *)d.xerr) return;
   const unsigned long long target = (*d.xepoch << 40) | ((unsigned long long)t + 1ull);
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(d.peer_flag[r] + d.rank), "l"(target) : "memory");
   unsigned long long start;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
   for (unsigned spin = 0; spin < (1u << 30); ++spin) {

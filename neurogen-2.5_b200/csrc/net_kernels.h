@@ -45,7 +45,6 @@ struct NetDev {
   uint32_t *const *peer_bm;
   unsigned long long *const *peer_flag;
   unsigned long long *xflag;    // this rank's flag array [world]
-  unsigned *xcount;             // [3]: CTAs of k_net_alif done with tick t's stores (by t % 3)
   int *xerr;                    // 1: a wait for a peer's flag ran out
   const unsigned long long *xepoch; // the exchange epoch (device memory, read by the kernels)
   int world, rank;
