@@ -25,6 +25,30 @@ def config(rank, world):
                           seed=12, part_rank=rank, part_world=world)
 
 
+def stall(out, rank, world, nccl_id):
+    """Failure path of the peer exchange: rank 1 stays between steps and never runs its ticks, so
+    rank 0's wait for its spikes runs out (2 s); rank 0's run must raise, and the same process must
+    then build and run a new network.  No kernel or collective of rank 1 is in flight meanwhile."""
+    import time
+    net = Network.partitioned(config(rank, world), nccl_id)
+    msg, took = '', 0.0
+    if rank == 0:
+        t0 = time.time()
+        try:
+            net.run(3)
+        except ValueError as e:
+            msg = str(e)
+        took = time.time() - t0
+        after = Network(config(0, 0))
+        _, c = after.run(20)
+        alive = int(c[:, 0].sum())
+        after.close()
+        np.savez(out / 'stall.npz', msg=np.array(msg), took=took, alive=alive, exchange=np.array(net.exchange))
+    dist.barrier()
+    net.close()
+    dist.destroy_process_group()
+
+
 def main():
     out = Path(sys.argv[1])
     rank, world, local = int(os.environ['RANK']), int(os.environ['WORLD_SIZE']), int(os.environ['LOCAL_RANK'])
@@ -33,6 +57,9 @@ def main():
     dist.init_process_group('gloo', timeout=datetime.timedelta(seconds=120))
     ids = [nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0)
+    if len(sys.argv) > 2 and sys.argv[2] == 'stall':
+        stall(out, rank, world, ids[0])
+        return
     net = Network.partitioned(config(rank, world), ids[0])
     spikes, counts = net.run(60)
     snap = net.get_state()              # tick 60

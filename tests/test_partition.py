@@ -110,3 +110,22 @@ def test_two_gpu_partition_equals_whole_network(tmp_path, exchange):
     ring = np.concatenate([r['ring'] for r in ranks], axis=1)
     assert np.array_equal(ring, full['ring'])
     assert ranks[0]['v'].shape[0] == half
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason='needs two GPUs')
+def test_two_gpu_exchange_wait_runs_out_cleanly(tmp_path):
+    """The peer exchange's wait is bounded: when one rank never runs its ticks (it stays between
+    steps, nothing of it in flight), the other rank's wait gives up after its 2 s limit, the run
+    raises, and the process goes on to build and run a new network on the same GPU."""
+    env = dict(os.environ, MASTER_ADDR='127.0.0.1', NCCL_NVLS_ENABLE='0', NEUROGEN_PEER_EXCHANGE='1')
+    cmd = ['timeout', '-k', '30', '300', sys.executable, '-m', 'torch.distributed.run', '--nnodes=1',
+           '--nproc-per-node=2', '--master-addr', '127.0.0.1', '--master-port', '29645',
+           str(ROOT / 'tests' / 'net_partition_worker.py'), str(tmp_path), 'stall']
+    out = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert out.returncode == 0, out.stderr[-4000:]
+    r = np.load(tmp_path / 'stall.npz')
+    assert str(r['exchange']) == 'peer'
+    assert 'timed out' in str(r['msg']), str(r['msg'])
+    assert 1.5 < float(r['took']) < 60.0
+    assert int(r['alive']) > 0
