@@ -299,15 +299,15 @@ def tick_traffic(workload, mode, rate):
 KERNEL_OF_LAUNCH = {'fused': 'k_net_fused', 'split': 'tick = k_net_alif + k_net_push',
                     'resident': 'k_net_resident (persistent, serial tick, 2,048 ticks a launch)',
                     'resident-pipelined': 'k_net_pipe (persistent, pipelined tick, 2,048 ticks a launch)',
-                    'split-learning': 'tick = k_net_alif + k_net_learn + k_net_post + k_net_push'}
+                    'split-learning': 'tick = k_net_alif + k_net_learn + k_net_push'}
 
 
 def tick_launches(mode, ticks):
     """Kernels the engine launches for one run of `ticks` ticks without per-tick outputs."""
     if mode.startswith('resident'):
         return -(-ticks // 2048)
-    # split: membrane, delay-1 push, delay>=2 push; learning: membrane, learn, post trace, push
-    per_tick = 1 if mode == 'fused' else 4 if mode == 'split-learning' else 3
+    # split: membrane, delay-1 push, delay>=2 push; learning: membrane, learn, push
+    per_tick = 1 if mode == 'fused' else 3
     graphs = ticks // 64
     return graphs * (64 * per_tick + 1) + (ticks - graphs * 64) * per_tick + (1 if graphs else 0)
 

@@ -1107,7 +1107,7 @@ void Network::launch_tick(TickRef t, int parity, uint32_t *spikes_row, unsigned 
                           cudaStream_t st) {
   if (split_) {
     launch_membrane(t, parity, spikes_row, counts_row, st);
-    if (dev_.pre_tr) launch_net_learn(dev_, t, st); // learn before the tick's emissions
+    if (dev_.pre_tr) launch_net_learn(dev_, t, st); // learn before the tick's emissions (post traces: the push)
     launch_net_push(dev_, t, counts_row, 0, st);
   } else {
     launch_net_fused(dev_, t, spikes_row, counts_row, st);

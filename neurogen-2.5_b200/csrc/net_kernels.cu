@@ -283,7 +283,8 @@ __global__ void k_net_xwait(NetDev d, TickRef tr) {
 // from the history (bit j: tick t - j), so a contact of delay d sees its
 // arrival as bit d; the lanes then take the row's contacts 32 at a time.
 // Zero-weight entries (row padding) are not contacts.  The post trace of every
-// neuron is decayed and advanced after all contacts have read it (k_net_post).
+// neuron is decayed and advanced after all contacts have read it, by the
+// tick's push (k_net_push, whole rows).
 // ---------------------------------------------------------------------------
 // One contact's learning step (the fp32 contract); a = arrival, post = postsynaptic spike.
 __device__ __forceinline__ void learn_contact(const NetDev &d, bool exc, int q, float a, float post, float &w_io,
@@ -357,14 +358,6 @@ __global__ void __launch_bounds__(TB) k_net_learn(NetDev d, TickRef tr) {
   }
 }
 
-__global__ void __launch_bounds__(TB) k_net_post(NetDev d, TickRef tr) {
-  const long long t = tick_of(tr);
-  const int i = blockIdx.x * TB + threadIdx.x;
-  if (i >= d.n) return;
-  const uint32_t *now = d.hist + (t & (kRingSlots - 1)) * d.bm_stride;
-  const float s = ((now[i >> 5] >> (i & 31)) & 1u) ? 1.f : 0.f;
-  d.post_tr[i] = __fadd_rn(__fmul_rn(d.post_tr[i], d.l_decay), s);
-}
 
 // CTA b pushes the spikes of presynaptic neurons [32*SPANW*b, 32*SPANW*(b+1)):
 // warp 0 lists them from the span's SPANW bitmask words (block storage: 8
@@ -383,6 +376,15 @@ __global__ void __launch_bounds__(TB) k_net_push(NetDev d, TickRef tr, unsigned 
   const uint32_t *bitmask = d.bitmask + (t % d.bm_bufs) * d.bm_stride;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int base = blockIdx.x * SPAN;
+  if (SEG == 0 && d.post_tr) {
+    // Learning networks: the post traces of this span's neurons, decayed and
+    // advanced by this tick's spikes once every contact has read them
+    // (k_net_learn, the previous launch).
+    for (int i = base + threadIdx.x; i < min(base + SPAN, d.n); i += TB) {
+      const float sp = ((bitmask[i >> 5] >> (i & 31)) & 1u) ? 1.f : 0.f;
+      d.post_tr[i] = __fadd_rn(__fmul_rn(d.post_tr[i], d.l_decay), sp);
+    }
+  }
   if (warp == 0) {
     if (BSR) {
       const int w = base / 32 + (lane & 7);
@@ -448,7 +450,6 @@ void launch_net_xwait(const NetDev &d, TickRef t, cudaStream_t s) { k_net_xwait<
 
 void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s) {
   if (d.n_pre > 0) k_net_learn<<<(d.n_pre + 2 * WARPS - 1) / (2 * WARPS), TB, 0, s>>>(d, t);
-  if (d.n > 0) k_net_post<<<(d.n + TB - 1) / TB, TB, 0, s>>>(d, t);
 }
 
 template <bool BSR, int SPANW, int CH>

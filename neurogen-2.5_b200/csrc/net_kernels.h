@@ -93,8 +93,8 @@ void launch_net_xwait(const NetDev &d, TickRef t, cudaStream_t s);
 // seg: 0 whole rows, 1 delay-1 segments only, 2 delay>=2 segments only.
 void launch_net_push(const NetDev &d, TickRef t, unsigned long long *counts, int seg, cudaStream_t s);
 // Learning of tick t (plasticity networks), after k_net_alif and before the
-// push: every contact's weight and traces (biology.py:182-218), then every
-// neuron's post trace.
+// push: every contact's weight and traces (biology.py:182-218).  The push of
+// the tick (whole rows) then advances every neuron's post trace.
 void launch_net_learn(const NetDev &d, TickRef t, cudaStream_t s);
 constexpr int kTotalsStride = 3;
 constexpr int kNetBlock = 256; // neurons per membrane CTA
