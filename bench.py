@@ -275,9 +275,10 @@ def tick_bytes(cfg, spikes, events, held=None, contacts=0):
         return per_neuron + spikes * cfg.bsr_blocks * 36
     learning = 0
     if cfg.plasticity and contacts:
-        # Every contact every tick: index read, weight and four traces read and written (44 B);
-        # every neuron: post trace and rate read and written (16 B) and its history bit.
-        learning = contacts * 44 + held * 16 + held / 8
+        # Every contact every tick: index read, weight and three traces read and written (36 B;
+        # a stored contact's potential trace is its pre trace); every neuron: post trace and rate
+        # read and written (16 B) and its history bit.
+        learning = contacts * 36 + held * 16 + held / 8
     return per_neuron + events * (4 + wbytes + 1) + learning
 
 

@@ -914,7 +914,7 @@ void Network::init_learning(size_t bm_words) {
   long long entries = 0;
   NGB_CUDA(cudaMemcpy(&entries, dev_.row + n_pre_, 8, cudaMemcpyDeviceToHost));
   const size_t E = size_t(std::max<long long>(entries, 1)), N = size_t(n_);
-  for (DeviceBuffer *b : {&pre_tr_, &pot_tr_, &coact_, &usage_}) {
+  for (DeviceBuffer *b : {&pre_tr_, &coact_, &usage_}) {
     b->reset(E * 4);
     NGB_CUDA(cudaMemset(b->as<void>(), 0, E * 4));
   }
@@ -926,7 +926,6 @@ void Network::init_learning(size_t bm_words) {
   NGB_CUDA(cudaMemset(hist_.as<void>(), 0, size_t(kRingSlots) * bm_words * 4));
   NetDev &d = dev_;
   d.pre_tr = pre_tr_.as<float>();
-  d.pot_tr = pot_tr_.as<float>();
   d.coact = coact_.as<float>();
   d.usage = usage_.as<float>();
   d.post_tr = post_tr_.as<float>();
@@ -959,7 +958,8 @@ void Network::plasticity_state(float *pre_tr, float *pot_tr, float *coact, float
   const size_t E = size_t(row[n_pre_]);
   std::vector<float> w(E), buf(E);
   if (E) NGB_CUDA(cudaMemcpy(w.data(), w_.as<void>(), E * 4, cudaMemcpyDeviceToHost));
-  const float *src[4] = {dev_.pre_tr, dev_.pot_tr, dev_.coact, dev_.usage};
+  // The potential trace of a stored contact is its pre trace.
+  const float *src[4] = {dev_.pre_tr, dev_.pre_tr, dev_.coact, dev_.usage};
   float *dst[4] = {pre_tr, pot_tr, coact, usage};
   for (int k = 0; k < 4; ++k) {
     if (!dst[k] || !E) continue;

@@ -107,7 +107,7 @@ private:
   DeviceBuffer v_, a_, ge_, gi_, ref_, ring_;
   DeviceBuffer rec_spikes_, rec_counts_;
   DeviceBuffer bitmask_, totals_, tick_dev_;
-  DeviceBuffer pre_tr_, pot_tr_, coact_, usage_, post_tr_, rate_, scale_, hist_; // learning
+  DeviceBuffer pre_tr_, coact_, usage_, post_tr_, rate_, scale_, hist_; // learning
   void init_learning(size_t bm_words);
   // One-sided spike exchange (partitioned networks).
   DeviceBuffer xbuf_, peer_bm_, peer_flag_, xctl_;

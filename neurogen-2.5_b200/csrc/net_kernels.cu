@@ -287,10 +287,13 @@ __global__ void k_net_xwait(NetDev d, TickRef tr) {
 // tick's push (k_net_push, whole rows).
 // ---------------------------------------------------------------------------
 // One contact's learning step (the fp32 contract); a = arrival, post = postsynaptic spike.
+// A stored contact's potential arrival is its arrival (biology.py:141-146 for
+// an active contact), so its potential trace equals its pre trace at every
+// tick: one array holds both.
 __device__ __forceinline__ void learn_contact(const NetDev &d, bool exc, int q, float a, float post, float &w_io,
-                                              float &pre_tr, float &pot_tr, float &coact, float &usage) {
+                                              float &pre_tr, float &coact, float &usage) {
   const float pt = __fmul_rn(pre_tr, d.l_decay);
-  const float pot = __fmul_rn(pot_tr, d.l_decay);
+  const float pot = pt;
   const float pq = __fmul_rn(d.post_tr[q], d.l_decay);
   float w = fabsf(w_io);
   if (d.learn_weights) {
@@ -311,7 +314,6 @@ __device__ __forceinline__ void learn_contact(const NetDev &d, bool exc, int q, 
   coact = __fadd_rn(__fmul_rn(coact, d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, pot), post));
   usage = __fadd_rn(__fmul_rn(usage, d.l_slow), __fmul_rn(__fmul_rn(d.l_oms, a), d.l_per_ms));
   pre_tr = __fadd_rn(pt, a);
-  pot_tr = __fadd_rn(pot, a);
   w_io = w_io < 0.f ? -w : w;
 }
 
@@ -336,10 +338,9 @@ __global__ void __launch_bounds__(TB) k_net_learn(NetDev d, TickRef tr) {
     if (w4.x == 0.f && w4.y == 0.f && w4.z == 0.f && w4.w == 0.f) continue; // row padding
     const uint4 s4 = *reinterpret_cast<const uint4 *>(d.syn + e);
     float4 pr = *reinterpret_cast<const float4 *>(d.pre_tr + e);
-    float4 po = *reinterpret_cast<const float4 *>(d.pot_tr + e);
     float4 co = *reinterpret_cast<const float4 *>(d.coact + e);
     float4 us = *reinterpret_cast<const float4 *>(d.usage + e);
-    float *wv = &w4.x, *prv = &pr.x, *pov = &po.x, *cov = &co.x, *usv = &us.x;
+    float *wv = &w4.x, *prv = &pr.x, *cov = &co.x, *usv = &us.x;
     const uint32_t words[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -348,11 +349,10 @@ __global__ void __launch_bounds__(TB) k_net_learn(NetDev d, TickRef tr) {
       const int dly = (int)(words[j] >> 28) + 1;
       const float a = ((past >> dly) & 1u) ? 1.f : 0.f;
       const float post = ((now[q >> 5] >> (q & 31)) & 1u) ? 1.f : 0.f;
-      learn_contact(d, exc, q, a, post, wv[j], prv[j], pov[j], cov[j], usv[j]);
+      learn_contact(d, exc, q, a, post, wv[j], prv[j], cov[j], usv[j]);
     }
     *reinterpret_cast<float4 *>(w32 + e) = w4;
     *reinterpret_cast<float4 *>(d.pre_tr + e) = pr;
-    *reinterpret_cast<float4 *>(d.pot_tr + e) = po;
     *reinterpret_cast<float4 *>(d.coact + e) = co;
     *reinterpret_cast<float4 *>(d.usage + e) = us;
   }

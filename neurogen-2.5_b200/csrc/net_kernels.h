@@ -63,9 +63,10 @@ struct NetDev {
   unsigned long long drive_key;
   int ref_ticks;
   // Learning (plasticity networks; null pointers otherwise): per CSR entry the
-  // pre trace, potential trace, coactivity and usage; per neuron the post trace
-  // and the rate; the spike bitmask of the last kRingSlots ticks [16][bm_stride].
-  float *pre_tr, *pot_tr, *coact, *usage, *post_tr, *rate;
+  // pre trace (equal to the potential trace for a stored contact), coactivity
+  // and usage; per neuron the post trace and the rate; the spike bitmask of the
+  // last kRingSlots ticks [16][bm_stride].
+  float *pre_tr, *coact, *usage, *post_tr, *rate;
   float *scale;   // per neuron, this tick: the synaptic-scaling factor of its E contacts
   uint32_t *hist;
   int learn_weights; // 1: weights learn (0: traces only)
