@@ -147,7 +147,7 @@ void *ng_pool_create(void *engine, int batch) {
     pool->logits.reset(size_t(batch) * kVocab * 4);
     pool->hidden.reset(size_t(batch) * e->config.width * 4);
     pool->act.reset(size_t(batch) * 4);
-    pool->sc.ensure(m.dims, batch);
+    pool->sc.ensure(m.dims, batch, m.tc_proj);
     NGB_CUDA(cudaStreamCreateWithFlags(&pool->stream, cudaStreamNonBlocking));
     return pool.release();
   });

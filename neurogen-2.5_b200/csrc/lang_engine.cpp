@@ -80,7 +80,7 @@ LangDims::LangDims(const EngineConfig &cfg, const CorticalColumnV2 &col)
   S = static_cast<long>(R) * RS;
 }
 
-void Scratch::ensure(const LangDims &d, int batch) {
+void Scratch::ensure(const LangDims &d, int batch, bool tc_proj) {
   if (batch <= capacity) return;
   const size_t B = batch;
   h.reset(B * d.w * 4);
@@ -98,6 +98,11 @@ void Scratch::ensure(const LangDims &d, int batch) {
   act.reset(B * 4);
   h_hi.reset(B * d.w * 4);
   h_lo.reset(B * d.w * 4);
+  if (tc_proj) {
+    const size_t kmax = std::max<size_t>(d.w, size_t(d.c) * d.n_out * 2);
+    x_hi.reset(B * kmax * 4);
+    x_lo.reset(B * kmax * 4);
+  }
   capacity = batch;
 }
 
@@ -157,6 +162,22 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   // Recurrent connectivity gain [post][pre] (laminar rule, no autapses).
   const std::vector<float> rec_gain = col.recurrent_gain();
 
+  // tf32 split of a row-major matrix: hi = x with the low 13 mantissa bits
+  // cleared (a tf32 value), lo = x - hi (exact in fp32).
+  auto split_upload = [](const float *x, size_t count, DeviceBuffer &hi_dev, DeviceBuffer &lo_dev) {
+    std::vector<float> hi(count), lo(count);
+    for (size_t i = 0; i < count; ++i) {
+      uint32_t bits;
+      std::memcpy(&bits, x + i, 4);
+      bits &= 0xFFFFE000u;
+      std::memcpy(&hi[i], &bits, 4);
+      lo[i] = x[i] - hi[i];
+    }
+    hi_dev = upload(hi);
+    lo_dev = upload(lo);
+  };
+  tc_proj = projection_tc_enabled();
+
   const float *p = data;
   auto take = [&](size_t count) {
     const float *start = p;
@@ -182,13 +203,16 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
     const float *in_w = take(c * d.n_in * w);
     g.in_wp = upload(to_panels(in_w, c * d.n_in, w));
     g.in_wr = upload(in_w, c * d.n_in * w);
+    if (tc_proj) split_upload(in_w, c * d.n_in * w, g.in_hi, g.in_lo);
     g.in_b = upload(take(c * d.n_in), c * d.n_in);
     const float *fb_w = take(c * d.n_fb * w);
     g.fb_wp = upload(to_panels(fb_w, c * d.n_fb, w));
     g.fb_wr = upload(fb_w, c * d.n_fb * w);
+    if (tc_proj) split_upload(fb_w, c * d.n_fb * w, g.fb_hi, g.fb_lo);
     const float *out_w = take(w * c * d.n_out * 2);
     g.out_wp = upload(to_panels(out_w, w, c * d.n_out * 2));
     g.out_wr = upload(out_w, w * c * d.n_out * 2);
+    if (tc_proj) split_upload(out_w, w * c * d.n_out * 2, g.out_hi, g.out_lo);
     g.out_b = upload(take(w), w);
     g.norm_w = upload(take(w), w);
     g.norm_b = upload(take(w), w);
@@ -200,18 +224,7 @@ DeviceModel::DeviceModel(const EngineConfig &cfg, const CorticalColumnV2 &col, c
   const float *head_w = take(size_t(kVocab) * w);
   head_wp = upload(to_panels(head_w, kVocab, w));
   head_wr = upload(head_w, size_t(kVocab) * w);
-  {
-    std::vector<float> hi(size_t(kVocab) * w), lo(hi.size());
-    for (size_t i = 0; i < hi.size(); ++i) {
-      uint32_t bits;
-      std::memcpy(&bits, head_w + i, 4);
-      bits &= 0xFFFFE000u;
-      std::memcpy(&hi[i], &bits, 4);
-      lo[i] = head_w[i] - hi[i]; // exact in fp32
-    }
-    head_hi = upload(hi);
-    head_lo = upload(lo);
-  }
+  split_upload(head_w, size_t(kVocab) * w, head_hi, head_lo);
   head_b = upload(take(kVocab), kVocab);
   NGB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   NGB_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&readout_err), sizeof(int), cudaHostAllocMapped));
@@ -247,6 +260,21 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
   const ReadoutArgs ra{sc.h_hi, sc.h_lo, d.w, head_hi.as<float>(), head_lo.as<float>(), head_b.as<float>(),
                        d_logits, kVocab, B, d.w, kVocab, readout_err_dev};
   const bool tc_readout = d_logits && readout_tc_ok(ra);
+  // A projection on the tensor cores (NEUROGEN_PROJECTION=tc, B >= 2): its
+  // input split into tf32 hi / lo, then the readout kernel with the
+  // projection's weights; the exact sequential kernel otherwise.
+  const bool tc_proj_here = tc_proj && B >= 2 && sc.x_hi && sc.x_lo;
+  auto project = [&](const ProjArgs &pa, const DeviceBuffer &w_hi, const DeviceBuffer &w_lo) {
+    if (tc_proj_here) {
+      launch_tf32_split(pa.x, pa.xidx, pa.ldx, pa.K, B, sc.x_hi, sc.x_lo, st);
+      ReadoutArgs a{sc.x_hi, sc.x_lo, pa.K, w_hi.as<float>(), w_lo.as<float>(), pa.bias, pa.y, pa.ldy,
+                    B, pa.K, pa.M, readout_err_dev};
+      a.addv = pa.addv;
+      a.ldadd = pa.ldadd;
+      if (launch_readout_tc(a, st)) return;
+    }
+    launch_projection(pa, st);
+  };
   for (int adv = 0; adv < A; ++adv) {
     const bool idle = adv > 0 || first_idle;
     // Feedback projections of every region read only that region's memory,
@@ -268,7 +296,11 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
         fa.K = d.w;
         fa.B = B;
       }
-      launch_projections(fb, st);
+      if (tc_proj_here) {
+        for (int z = 0; z < fb.count; ++z) project(fb.a[z], regions[r0 + z].fb_hi, regions[r0 + z].fb_lo);
+      } else {
+        launch_projections(fb, st);
+      }
     }
     for (int r = 0; r < d.R; ++r) {
       const RegionWeights &g = regions[r];
@@ -291,7 +323,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
         ia.M = Min;
         ia.K = d.w;
         ia.B = B;
-        launch_projection(ia, st);
+        project(ia, g.in_hi, g.in_lo);
       }
       TickArgs ta{};
       ta.rec = g.rec.as<float>();
@@ -338,7 +370,7 @@ void DeviceModel::enqueue_view(int B, const int *d_tokens, const float *d_inputs
       oa.M = d.w;
       oa.K = Kout;
       oa.B = B;
-      launch_projection(oa, st);
+      project(oa, g.out_hi, g.out_lo);
       NormArgs na{};
       na.hraw = sc.hraw;
       na.hraw_ld = d.w;
@@ -462,7 +494,7 @@ void NeuralEngine::step_batch(const int *tokens, int batch, const float *state, 
   DeviceModel &m = *impl_;
   NGB_CUDA(cudaSetDevice(m.device));
   Scratch &sc = m.host_scratch;
-  sc.ensure(m.dims, batch);
+  sc.ensure(m.dims, batch, m.tc_proj);
   cudaStream_t st = m.stream;
   NGB_CUDA(cudaMemcpyAsync(sc.tokens.as<int>(), tokens, batch * sizeof(int), cudaMemcpyHostToDevice, st));
   NGB_CUDA(cudaMemcpyAsync(sc.state.as<float>(), state, S * batch * 4, cudaMemcpyHostToDevice, st));
@@ -489,7 +521,7 @@ void NeuralEngine::advance_batch(const float *inputs, int batch, const float *st
   DeviceModel &m = *impl_;
   NGB_CUDA(cudaSetDevice(m.device));
   Scratch &sc = m.host_scratch;
-  sc.ensure(m.dims, batch);
+  sc.ensure(m.dims, batch, m.tc_proj);
   cudaStream_t st = m.stream;
   NGB_CUDA(cudaMemcpyAsync(sc.inputs.as<float>(), inputs, size_t(batch) * config.width * 4, cudaMemcpyHostToDevice, st));
   NGB_CUDA(cudaMemcpyAsync(sc.state.as<float>(), state, S * batch * 4, cudaMemcpyHostToDevice, st));

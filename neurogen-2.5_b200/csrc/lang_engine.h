@@ -27,6 +27,8 @@ struct RegionWeights {
   DeviceBuffer fb_wp;                   // panels of [c*n_fb][w]
   DeviceBuffer out_wp, out_b;           // panels of [w][c*n_out*2], bias
   DeviceBuffer in_wr, fb_wr, out_wr;    // the same three row-major (small-batch kernel)
+  // tf32 hi / lo splits of the three row-major matrices (tensor-core projections only)
+  DeviceBuffer in_hi, in_lo, fb_hi, fb_lo, out_hi, out_lo;
   DeviceBuffer norm_w, norm_b, decay;   // [w]
 };
 
@@ -37,16 +39,18 @@ struct ScratchView {
   float *h, *hraw, *vin, *fb, *tr, *feat;
   int *cnt;
   float *h_hi = nullptr, *h_lo = nullptr; // tf32 split of h for the tensor-core readout, or null
+  float *x_hi = nullptr, *x_lo = nullptr; // [B][max K] tf32 split of a projection's input, or null
 };
 
 // Per-call device workspace for `capacity` sessions.
 struct Scratch {
   int capacity = 0;
-  DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act, h_hi, h_lo;
-  void ensure(const LangDims &d, int batch);
+  DeviceBuffer h, hraw, vin, fb, tr, feat, cnt, tokens, inputs, state, logits, hidden, act, h_hi, h_lo, x_hi, x_lo;
+  void ensure(const LangDims &d, int batch, bool tc_proj);
   ScratchView view() const {
-    return {h.as<float>(), hraw.as<float>(), vin.as<float>(), fb.as<float>(),
-            tr.as<float>(), feat.as<float>(), cnt.as<int>(), h_hi.as<float>(), h_lo.as<float>()};
+    return {h.as<float>(),   hraw.as<float>(), vin.as<float>(),  fb.as<float>(),  tr.as<float>(),
+            feat.as<float>(), cnt.as<int>(),    h_hi.as<float>(), h_lo.as<float>(), x_hi.as<float>(),
+            x_lo.as<float>()};
   }
 };
 
@@ -83,6 +87,9 @@ public:
   libm_match::MathTable sig_tab, sig_neg_tab, tanh_tab;
   DeviceBuffer emb, head_wp, head_b, head_wr;
   DeviceBuffer head_hi, head_lo; // tf32 split of head_wr for the tensor-core readout
+  // Batched projections on the tensor cores too (NEUROGEN_PROJECTION=tc at
+  // model load); the exact sequential projections otherwise.
+  bool tc_proj = false;
   std::vector<RegionWeights> regions;
   Scratch host_scratch; // used by the host-buffer entry points (under the engine mutex)
   // Error word of the tensor-core readout (pinned, mapped into the device):

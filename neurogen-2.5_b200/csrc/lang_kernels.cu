@@ -134,8 +134,9 @@ __device__ __forceinline__ void load_x(const float *p, float (&x)[TN]) {
 // Packed pairs of fp32 (sm_100 f32x2): each lane of add.rn.f32x2 is one IEEE
 // round-to-nearest fp32 add, so pairing two independent chains changes no
 // bit.  Products stay scalar __fmul_rn: a packed multiply feeding a packed add
-// is contracted into a fused multiply-add by the assembler (measured on
-// B200), which would change the rounding.
+// is contracted into a fused multiply-add by the assembler, even written as
+// mul.rn.f32x2 with the explicit rounding mode (both measured on B200: the
+// projections stop being bit-identical), which would change the rounding.
 typedef unsigned long long f32x2;
 __device__ __forceinline__ f32x2 pack2(float lo, float hi) {
   f32x2 r;

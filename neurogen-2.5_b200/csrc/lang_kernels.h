@@ -63,6 +63,10 @@ struct ReadoutArgs {
   // Test switch: non-zero makes the launch give up before it issues any copy
   // or MMA, as a wait that ran out would (set by launch_readout_tc only).
   int stall_test;
+  // Optional epilogue y[b][v] += 0.25f * addv[b * ldadd + v] (the output
+  // projection's memory term), after the bias and the k sum.
+  const float *addv;
+  long ldadd;
 };
 // False when NEUROGEN_READOUT=simt is set (the sequential SIMT projection is
 // then used at every batch size).
@@ -71,6 +75,13 @@ bool readout_tc_enabled();
 bool readout_tc_ok(const ReadoutArgs &a);
 // Launches when readout_tc_ok(a); returns false (nothing launched) otherwise.
 bool launch_readout_tc(const ReadoutArgs &a, cudaStream_t s);
+// tf32 split of B rows of K floats (row b of x at x + (xidx ? xidx[b] : b) * ldx)
+// into hi / lo [B][K], for a projection on the tensor cores.
+void launch_tf32_split(const float *x, const int *xidx, long ldx, int K, int B, float *hi, float *lo,
+                       cudaStream_t s);
+// True when NEUROGEN_PROJECTION=tc: batched projections (B >= 2) run on the
+// tensor cores as well (split-tf32, not bit-identical to the sequential sum).
+bool projection_tc_enabled();
 void configure_readout_tc();
 const void *readout_tc_kernel();
 // Per-device kernel attributes (dynamic shared memory); call once per device

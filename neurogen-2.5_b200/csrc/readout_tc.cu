@@ -266,6 +266,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           o[2] = __fadd_rn(o[2], seg[sg].z);
           o[3] = __fadd_rn(o[3], seg[sg].w);
         }
+      if (a.addv) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (v + e < a.V) o[e] = __fadd_rn(o[e], __fmul_rn(0.25f, a.addv[(long)b * a.ldadd + v + e]));
+      }
       float *y = a.y + (long)b * a.ldy + v;
       if (v + 4 <= a.V && (a.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0) {
         *reinterpret_cast<float4 *>(y) = make_float4(o[0], o[1], o[2], o[3]);
@@ -315,7 +320,28 @@ bool make_map(CUtensorMap *m, const float *p, long rows, long cols, long ld, int
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// hi = x with the low 13 mantissa bits cleared (a tf32 value), lo = x - hi
+// (exact in fp32); the same split k_norm writes for the readout.
+__global__ void k_tf32_split(const float *x, const int *xidx, long ldx, int K, float *hi, float *lo) {
+  const int b = blockIdx.y, k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  const float v = x[(long)(xidx ? xidx[b] : b) * ldx + k];
+  const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  hi[(long)b * K + k] = h;
+  lo[(long)b * K + k] = __fsub_rn(v, h);
+}
+
 } // namespace
+
+void launch_tf32_split(const float *x, const int *xidx, long ldx, int K, int B, float *hi, float *lo,
+                       cudaStream_t s) {
+  k_tf32_split<<<dim3((K + 255) / 256, B), 256, 0, s>>>(x, xidx, ldx, K, hi, lo);
+}
+
+bool projection_tc_enabled() {
+  const char *e = std::getenv("NEUROGEN_PROJECTION");
+  return e && std::strcmp(e, "tc") == 0;
+}
 
 bool readout_tc_enabled() {
   const char *e = std::getenv("NEUROGEN_READOUT");

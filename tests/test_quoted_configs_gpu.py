@@ -15,6 +15,9 @@ its fp32 oracle by construction.
   one device-resident pool, 16 tokens: every session against its own reference engine run;
   the pool's token readout runs on the tensor cores, so its logits are held to 1e-4 relative
   with a floor of 1e-4 of the row's largest logit.
+* The opt-in tensor-core projections (NEUROGEN_PROJECTION=tc), outside the exact contract: the
+  first token of the 256 sessions within the bars, and the sessions that leave the reference's
+  spike trajectory after it, by token (printed).
 """
 import os
 from concurrent.futures import ThreadPoolExecutor
@@ -180,3 +183,66 @@ def test_bc250_256_session_pool_16_tokens_vs_reference():
         print(f'256 sessions x {T} tokens: spikes exact, state 1e-5; worst |logit error| / row max {worst:.2e}')
     finally:
         lib.ng_pool_destroy(pool)
+
+
+def test_bc250_256_sessions_tensor_core_projections_opt_in(monkeypatch):
+    """NEUROGEN_PROJECTION=tc (opt-in, outside the exact contract): every batched projection on the
+    tensor cores with split-tf32 operands.  Each projection is within a few 1e-6 of the sequential
+    fp32 sum, so the first token's spikes are still exact and its logits within the readout bar;
+    after that a membrane potential within that distance of its threshold flips a spike and the
+    session's dynamics leave the reference's.  The count of diverged sessions per token is printed;
+    the test holds the first token to the bars and checks that the mode is engaged (logits differ
+    from the exact projections)."""
+    B, T = 256, 8
+    cfg = LanguageConfig()
+    w = init_packed_weights(cfg, seed=0)
+    toks = session_streams(B, T)
+
+    def run_pool(eng, t_count):
+        lib = eng.lib
+        pool = lib.ng_pool_create(eng.handle, B)
+        assert pool, lib.ng_error().decode()
+        out = []
+        try:
+            logits = np.zeros((B, 264), np.float32)
+            state = np.zeros((B, eng.state_size), np.float32)
+            for t in range(t_count):
+                assert lib.ng_pool_step(pool, np.ascontiguousarray(toks[t]), logits.ctypes.data, None, None) == 0, \
+                    lib.ng_error().decode()
+                assert lib.ng_pool_store(pool, state) == 0
+                out.append((logits.copy(), state.copy()))
+        finally:
+            lib.ng_pool_destroy(pool)
+        return out
+
+    exact = run_pool(NativeEngine(cfg, w), 1)
+    monkeypatch.setenv('NEUROGEN_PROJECTION', 'tc')
+    tc = run_pool(NativeEngine(cfg, w), T)
+
+    workers = max(1, min(32, os.cpu_count() or 1))
+    engines = [RefEngine(cfg, w) for _ in range(workers)]
+    ref_state = np.zeros((B, engines[0].S), np.float32)
+    ref_logits = np.zeros((B, 264), np.float32)
+
+    def ref_slice(k, t):
+        for b in range(k, B, workers):
+            ref_logits[b], ref_state[b], _, _ = engines[k].step(int(toks[t, b]), ref_state[b])
+
+    diverged = np.zeros(B, bool)
+    report = []
+    with ThreadPoolExecutor(workers) as ex:
+        for t in range(T):
+            list(ex.map(lambda k: ref_slice(k, t), range(workers)))
+            logits, state = tc[t]
+            for b in range(B):
+                if not diverged[b] and not spikes_equal(cfg, state[b], ref_state[b]):
+                    diverged[b] = True
+            if t == 0:
+                assert not diverged.any(), 'first token: spikes differ with tensor-core projections'
+                scale = np.abs(ref_logits).max(axis=1, keepdims=True)
+                err = np.abs(logits.astype(np.float64) - ref_logits) - LOGIT_RTOL * np.abs(ref_logits)
+                assert (err <= LOGIT_RTOL * scale).all(), 'first token: logits beyond 1e-4 (row floor)'
+                assert not np.array_equal(logits, exact[0][0]), 'tensor-core projections not engaged'
+            report.append(int(diverged.sum()))
+    print(f'tensor-core projections, {B} sessions: sessions with a spike differing from the reference, '
+          f'by token (4 ticks a token): {report}')
