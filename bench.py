@@ -11,8 +11,9 @@ Workloads (seeded synthetic inputs of the benchmark configurations):
   learn8k   the same network learning every tick (biology.py's STDP, inhibitory rule, synaptic
             scaling and traces on every contact; split launch shape).
   partitioned4m  N=4,194,304, fan-in 1,000, fp16, imposed Bernoulli(0.01), 1,000 ticks a step;
-            under torchrun the neurons are row-partitioned over the ranks with a per-tick NCCL
-            all-gather of the spike bitmask (one network: strong scaling).
+            under torchrun the neurons are row-partitioned over the ranks, which exchange the
+            tick's spike bitmask slices by one-sided peer stores over NVLink (NCCL all-gather when
+            a rank cannot map its peers; one network: strong scaling).
   bc250     BC-250 language core, seed-0 weights, batch 1, one step = 512 tokens.  tokens/s.
   sessions  BC-250, 256 independent sessions (split over the ranks: strong scaling), one step =
             64 tokens per session.  tokens/s.
@@ -239,7 +240,8 @@ def tick_config_dict(name, c, world, ticks):
             'learning': ('STDP + inhibitory rule + synaptic scaling + traces every tick'
                          if c.get('plasticity') else None),
             'l2': 'inputs larger than L2' if synapses * 6 > L2_BYTES else 'network fits in L2; L2 flushed between steps',
-            'parallelism': (f'rows{world} + NCCL bitmask all-gather' if part and world > 1 else
+            'parallelism': (f'rows{world} + spike bitmask exchange (one-sided peer stores over NVLink, '
+                            'NCCL all-gather fall-back)' if part and world > 1 else
                             'one GPU' if part else f'replicas{world}')}
 
 
@@ -377,7 +379,8 @@ def bench_ticks(name, args, dist, steps, warmup, cpu=True):
         'higher_is_better': True, 'scaling': 'strong' if part else 'weak', 'vs_baseline': None,
         'dtype': 'fp32', 'data': 'synthetic', 'config': tick_config_dict(name, oc, dist.world, ticks),
         'measured': {'spike_rate': spikes / total_ticks / cfg.n, 'events_per_tick': events / total_ticks,
-                     'launch': mode, 'resident_tick': net.resident_tick, 'setup_s': round(setup_s, 2)},
+                     'launch': mode, 'resident_tick': net.resident_tick, 'setup_s': round(setup_s, 2),
+                     'exchange': net.exchange if part and dist.world > 1 else None},
         'synaptic_events_per_s': events * (1 if part else dist.world) / t_max,
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak_total, 'unit': 'GB/s',
                      'frac': achieved / peak_total,
