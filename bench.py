@@ -603,7 +603,52 @@ def bench_lang(name, args, dist, steps, warmup, cpu=True):
         rec['cpu_baseline'] = cpu_baseline_lang(name, toks, budget_s=8.0)
     lib.ng_pool_destroy(pool)
     eng.close()
+    if name == 'sessions':
+        rec['tensor_core_projections'] = bench_lang_tc(cfg, w, d_tok, B, T, steps, warmup, dist, stream, flush)
     return rec
+
+
+def bench_lang_tc(cfg, w, d_tok, B, T, steps, warmup, dist, stream, flush):
+    """The same sessions with the opt-in tensor-core projections (NEUROGEN_PROJECTION=tc, read when
+    the engine is created): faster, but not spike-exact, so reported beside the exact figure."""
+    import torch
+    from neurogen_b200 import library
+    from neurogen_b200.language import NativeEngine
+    lib = library()
+    old = os.environ.get('NEUROGEN_PROJECTION')
+    os.environ['NEUROGEN_PROJECTION'] = 'tc'
+    try:
+        eng = NativeEngine(cfg, w)
+    finally:
+        if old is None:
+            del os.environ['NEUROGEN_PROJECTION']
+        else:
+            os.environ['NEUROGEN_PROJECTION'] = old
+    pool = lib.ng_pool_create(eng.handle, B)
+    if not pool:
+        raise RuntimeError(lib.ng_error().decode())
+    d_logits = torch.empty((B, 264), device='cuda')
+    pos = [0]
+
+    def step():
+        for _ in range(T):
+            row = d_tok[pos[0] % d_tok.shape[0]]
+            if lib.ng_pool_step_device(pool, row.data_ptr(), d_logits.data_ptr(), stream.cuda_stream):
+                raise RuntimeError(lib.ng_error().decode())
+            pos[0] += 1
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_max = dist.max(time_steps(step, stream, steps, flush))
+    lib.ng_pool_destroy(pool)
+    eng.close()
+    return {'value': B * T * steps * dist.world / t_max, 'unit': 'tokens/s', 'ms_per_step': t_max / steps * 1e3,
+            'switch': 'NEUROGEN_PROJECTION=tc',
+            'parity': ('not spike-exact: every batched projection on tcgen05 with split-tf32 operands, within '
+                       'a few 1e-6 of the exact sum; the first spike flips within a few ticks '
+                       '(tests/test_quoted_configs_gpu.py)')}
 
 
 def cpu_baseline_lang(name, toks, budget_s):
