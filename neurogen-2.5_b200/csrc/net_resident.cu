@@ -1137,7 +1137,10 @@ template <bool BSR, bool HALF> __global__ void __launch_bounds__(BT) k_owner_cou
 }
 
 // CTA per presynaptic row: writes its owner blocks (pre-filled with empty
-// words) and allocates overflow blocks from `cursor`.
+// words) and allocates the row's overflow blocks from `cursor` as one run,
+// the owner CTAs' chains in CTA order, so that the overflow blocks of a
+// spiking row, read by all its owner CTAs in the same tick, lie side by side
+// in memory as its primary blocks do.
 template <class E, bool BSR, bool HALF>
 __global__ void __launch_bounds__(BT) k_owner_fill(NetDev d, ResidentDev r, typename E::word *blocks,
                                                    unsigned long long *cursor, unsigned long long capacity,
@@ -1156,15 +1159,29 @@ __global__ void __launch_bounds__(BT) k_owner_fill(NetDev d, ResidentDev r, type
     if (owner_event<BSR, HALF>(d, r, pre, e))
       atomicAdd(&cnt[(int)(edge_word<BSR>(d, e) & kPostMask) / P], 1);
   __syncthreads();
-  for (int q = threadIdx.x; q < C; q += BT) {
-    const int m = chain_blocks(cnt[q]);
-    long long base = -1;
-    if (m) {
-      const unsigned long long b = atomicAdd(cursor, (unsigned long long)m);
-      if (b + m <= capacity) base = (long long)(primary + b);
-      else atomicExch(err, 2);
+  if (threadIdx.x < 32) {
+    // chain[q] = overflow blocks of owners before q (exclusive scan), then one allocation.
+    const int lane = threadIdx.x;
+    unsigned long long run = 0;
+    for (int q0 = 0; q0 < C; q0 += 32) {
+      const int q = q0 + lane;
+      const int m = q < C ? chain_blocks(cnt[q]) : 0;
+      int incl = m;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (q < C) chain[q] = (long long)run + (incl - m);
+      run += (unsigned long long)__shfl_sync(0xffffffffu, incl, 31);
     }
-    chain[q] = base;
+    unsigned long long b = 0;
+    if (lane == 0 && run) b = atomicAdd(cursor, run);
+    b = __shfl_sync(0xffffffffu, b, 0);
+    const bool fits = b + run <= capacity;
+    if (lane == 0 && run && !fits) atomicExch(err, 2);
+    for (int q = lane; q < C; q += 32)
+      chain[q] = (chain_blocks(cnt[q]) && fits) ? (long long)(primary + b) + chain[q] : -1;
   }
   __syncthreads();
   for (long long e = e0 + threadIdx.x; e < e1; e += BT) {
