@@ -905,8 +905,10 @@ void Network::check_exchange() {
 }
 
 // Learning buffers (biology.py:182-218): per CSR entry (padding included, never
-// read) four traces, per neuron the post trace and the rate, the spike history,
-// all zero; constants of the fp32 contract (oracle/net_oracle.c lc_of).
+// read) the pre trace (a stored contact's potential trace is the same value),
+// coactivity and usage; per neuron the post trace, the rate and the scaling
+// factor; the spike history; all zero.  Constants of the fp32 contract
+// (oracle/net_oracle.c lc_of).
 void Network::init_learning(size_t bm_words) {
   const ng_net_config &c = cfg;
   if (!dev_.row || dev_.bsr || (dev_.w_half && nnz_ > 0))
