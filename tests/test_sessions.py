@@ -78,3 +78,22 @@ def test_bench_algorithmic_bytes_per_tick():
     assert bench.tick_bytes(bsr, spikes, spikes * 512) == n * 48 + n / 8 + spikes * 128 * 36
     assert abs(bench.tick_bytes(csr, spikes, spikes * 512) / 1e6 - 40.8) < 0.1
     assert abs(bench.tick_bytes(bsr, spikes, spikes * 512) / 1e6 - 48.9) < 0.1
+
+
+def test_bench_learning_bytes_per_tick():
+    """The learning workload's roofline numerator adds, per contact, the index read and the weight
+    and three traces read and written (36 B: a stored contact's potential trace is its pre trace), and
+    per neuron the post trace and rate read and written (16 B) and its history bit; the network part
+    is the isolated tick's (fp32 weights: 9 B an event)."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location('bench', Path(__file__).resolve().parents[1] / 'bench.py')
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = bench.engine_config(bench.oracle_tick_config('learn8k', 0.0))
+    assert cfg.plasticity and cfg.weight_kind != 1
+    n = cfg.n
+    spikes, events, contacts = 0.02 * n, 0.02 * n * 164, 1_342_177
+    base = bench.tick_bytes(cfg, spikes, events)
+    assert base == n * 48 + n / 8 + events * 9
+    assert bench.tick_bytes(cfg, spikes, events, contacts=contacts) - base == contacts * 36 + n * 16 + n / 8
