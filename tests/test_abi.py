@@ -95,3 +95,16 @@ def test_no_gpu_fails_loudly():
     assert not create(cfg, w)
     msg = lib.ng_error().decode()
     assert 'CUDA' in msg or 'sm_100' in msg
+
+
+@pytest.mark.skipif(gpu_available(), reason='checks the no-GPU failure path')
+def test_no_gpu_network_fails_loudly():
+    """The network engine has no CPU path either: creating a network, or one from an edge list,
+    without an sm_100 device fails with a message and no handle."""
+    from neurogen_b200.network import Network, default_config
+    cfg = default_config(n=64, n_exc=51)
+    with pytest.raises(ValueError, match='CUDA|sm_100'):
+        Network(cfg)
+    edges = (np.array([0, 1]), np.array([1, 2]), np.array([1, 2]), np.array([0.5, 0.25]))
+    with pytest.raises(ValueError, match='CUDA|sm_100'):
+        Network(cfg, edges)
