@@ -157,10 +157,13 @@ struct LinkQueue {
 
 // One owner block a lane: all 8 slots decoded and delivered unconditionally
 // (predicated, no early exit), so a lane's 8 deliveries are independent of one
-// another; an overflow link is queued.  Returns the lane's event count.
+// another; an overflow link is queued, in `spill` when `links` is full (a
+// chain walked in place would hold up the lane's whole warp for a dependent
+// read).  Returns the lane's event count.
 template <class E>
 __device__ __forceinline__ int deliver_lane(const RingAt &ra, const typename E::word *blocks,
-                                            const typename E::word (&w)[kSlots], const LinkQueue &links) {
+                                            const typename E::word (&w)[kSlots], const LinkQueue &links,
+                                            const LinkQueue *spill = nullptr) {
   using W = typename E::word;
   int n = 0;
 #pragma unroll
@@ -177,14 +180,22 @@ __device__ __forceinline__ int deliver_lane(const RingAt &ra, const typename E::
   }
   const W last = w[kSlots - 1];
   if (last != E::kEmpty && (last & E::kLink)) {
+    const int link = (int)(last & ~E::kLink);
     const int at = atomicAdd(links.n, 1);
     if (at < links.cap) {
-      links.q[at] = (int)(last & ~E::kLink);
-    } else {
-      W b[kSlots];
-      load_block<E>(blocks + (size_t)(last & ~E::kLink) * kSlots, b);
-      n += deliver_block<E>(ra, blocks, b);
+      links.q[at] = link;
+      return n;
     }
+    if (spill) {
+      const int at2 = atomicAdd(spill->n, 1);
+      if (at2 < spill->cap) {
+        spill->q[at2] = link;
+        return n;
+      }
+    }
+    W b[kSlots];
+    load_block<E>(blocks + (size_t)link * kSlots, b);
+    n += deliver_block<E>(ra, blocks, b);
   }
   return n;
 }
@@ -417,12 +428,13 @@ __global__ void __launch_bounds__(RT, 1) k_net_resident(NetDev d, ResidentDev r,
         if (m + ph < M) {
           fetch(pn, b[(ph + D) % (D + 1)]); // round m + ph + D
           pn = list_at(m + ph + D + 1);
-          tick_events += (unsigned long long)deliver_lane<E>(ra, blocks, b[ph], own_links);
+          tick_events += (unsigned long long)deliver_lane<E>(ra, blocks, b[ph], own_links, &links0);
         }
       }
     }
     // The overflow blocks this warp met, delivered by the warp itself while the
-    // others may still be in their rounds; their own links go to the CTA queue.
+    // others may still be in their rounds; their own links, and those its full
+    // queue spilled, go to the CTA queue.
     __syncwarp();
     {
       const int n = min(warp_n_s[warp], kWarpLinks);
