@@ -288,7 +288,7 @@ def tick_bytes(cfg, spikes, events, held=None, contacts=0):
 # dominant kernel on this workload (profiles/k_net_resident_scaled_tick_262144_{csr,bsr16}.md: 64 ticks
 # at a 3% spike rate).  Owner-block traffic is proportional to the spikes, so it is scaled by the run's rate.
 NCU_TRAFFIC = {('scaled_tick_262144_csr', 'resident'): (2.400492e9 + 4.731392e6, 64, 0.030017),
-               ('scaled_tick_262144_bsr16', 'resident'): (2.697827e9 + 7.34336e6, 64, 0.030017)}
+               ('scaled_tick_262144_bsr16', 'resident'): (2.698401e9 + 4.773888e6, 64, 0.030017)}
 
 
 def tick_traffic(workload, mode, rate):
